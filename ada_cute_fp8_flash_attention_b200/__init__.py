@@ -1,0 +1,88 @@
+"""B200-native (sm_100a) FP8 flash-attention forward.
+
+Drop-in for the module ``ada_cute_fp8_flash_attention`` of
+Lemon7-UP/ada_cute_fp8_flash_attention, whose only export is
+``flash_attn_fp8_forward(q, k, v)`` (csrc/attention_api.cpp:6-9):
+
+* ``q``, ``k``: ``torch.float8_e4m3fn`` of shape (B, H, S, D), D in {64, 128};
+* ``v``: ``torch.float8_e4m3fn`` pre-transposed to (B, H, D, S) (test.py:51-52);
+* causal attention with scale 1/sqrt(D) (csrc/flash_attention.cu:524);
+* returns fp16 O of shape (B, H, S, D).
+
+The computation runs in the native library ``libfa8.so`` (C ABI,
+``include/fa8.h``) through the PyTorch extension ``_fa8_torch``. There is no
+CPU or eager-PyTorch fallback: importing this package raises ImportError when
+the native extension has not been built (``python -m
+ada_cute_fp8_flash_attention_b200._build``).
+"""
+from __future__ import annotations
+
+import importlib.util
+import sys
+
+from . import _build
+
+__all__ = [
+    "flash_attn_fp8_forward",
+    "flash_attn_fp8_forward_ex",
+    "lse_merge",
+    "quantize_e4m3",
+    "launch_count",
+]
+
+
+def _load_ext():
+    path = _build.ext_path()
+    if not path.exists():
+        raise ImportError(
+            f"native extension {path.name} is not built; run "
+            "`python -m ada_cute_fp8_flash_attention_b200._build` (no CPU fallback exists)")
+    import torch  # noqa: F401  (loads libc10 / libtorch for the extension)
+
+    name = f"{__name__}.{_build.EXT_NAME}"
+    spec = importlib.util.spec_from_file_location(name, str(path))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    sys.modules[name] = mod
+    return mod
+
+
+_C = _load_ext()
+
+
+def flash_attn_fp8_forward(q, k, v):
+    """Reference-compatible entry point: causal FP8 attention, V in (B,H,D,S), fp16 out."""
+    return _C.flash_attn_fp8_forward(q, k, v)
+
+
+def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout="bhds",
+                              return_lse=False, out_dtype="fp16", q_offset=0, kv_offset=0,
+                              split_keys=-1, out=None, lse=None):
+    """FP8 attention forward with options.
+
+    Returns ``out`` or ``(out, lse)`` when ``return_lse`` is set. ``lse`` is the
+    natural-log log-sum-exp of the scaled scores per query row (fp32, (B,H,S)),
+    ``-inf`` for rows with no visible key. ``q_offset``/``kv_offset`` are global
+    positions used by the causal mask (context-parallel chunks). ``split_keys``:
+    query tiles whose first row sees fewer keys than this use a two-term (hi +
+    lo) e4m3 P; -1 = default (1024), 0 = never.
+    """
+    res = _C.flash_attn_fp8_forward_ex(q, k, v, causal, softmax_scale, v_layout, return_lse,
+                                       out_dtype, q_offset, kv_offset, split_keys, out, lse)
+    return (res[0], res[1]) if return_lse else res[0]
+
+
+def lse_merge(outs, lses):
+    """Merge partial outputs of the same rows: returns (fp16 out, fp32 lse)."""
+    o, l = _C.lse_merge(list(outs), list(lses))
+    return o, l
+
+
+def quantize_e4m3(x, scale=1.0, transpose_last2=False):
+    """fp16/bf16 -> e4m3 (RNE, saturating at +-448), optionally transposing the last 2 dims."""
+    return _C.quantize_e4m3(x, scale, transpose_last2)
+
+
+def launch_count():
+    """Kernel launches issued through the C ABI by this process."""
+    return _C.launch_count()

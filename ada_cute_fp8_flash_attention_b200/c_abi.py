@@ -1,0 +1,117 @@
+"""ctypes binding of the C ABI in ``include/fa8.h`` (``libfa8.so``).
+
+This is the binding a non-torch caller (or a test) uses to reach the kernels
+without the PyTorch extension: plain pointers, sizes and integer status
+codes. ``Fa8FwdParams`` mirrors ``struct fa8_fwd_params`` field for field.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+from . import _build
+
+FA8_OK = 0
+FA8_ERR_INVALID_ARG = 1
+FA8_ERR_UNSUPPORTED = 2
+FA8_ERR_ALIGNMENT = 3
+FA8_ERR_CUDA = 4
+FA8_ERR_DRIVER = 5
+FA8_ERR_NO_DEVICE = 6
+FA8_V_BHDS = 0
+FA8_V_BHSD = 1
+FA8_OUT_F16 = 0
+FA8_OUT_E4M3 = 1
+
+# Every symbol include/fa8.h declares.
+EXPORTED = [
+    "fa8_fwd_params_init",
+    "fa8_fwd",
+    "fa8_lse_merge",
+    "fa8_quantize_e4m3",
+    "fa8_status_string",
+    "fa8_last_error_message",
+    "fa8_launch_count",
+]
+
+
+class Fa8FwdParams(C.Structure):
+    _fields_ = [
+        ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("o", C.c_void_p),
+        ("lse", C.c_void_p), ("status", C.c_void_p),
+        ("batch", C.c_int64), ("heads", C.c_int64), ("heads_kv", C.c_int64),
+        ("seqlen_q", C.c_int64), ("seqlen_kv", C.c_int64), ("head_dim", C.c_int64),
+        ("q_stride_b", C.c_int64), ("q_stride_h", C.c_int64), ("q_stride_s", C.c_int64),
+        ("k_stride_b", C.c_int64), ("k_stride_h", C.c_int64), ("k_stride_s", C.c_int64),
+        ("v_stride_b", C.c_int64), ("v_stride_h", C.c_int64), ("v_stride_r", C.c_int64),
+        ("o_stride_b", C.c_int64), ("o_stride_h", C.c_int64), ("o_stride_s", C.c_int64),
+        ("lse_stride_b", C.c_int64), ("lse_stride_h", C.c_int64),
+        ("softmax_scale", C.c_float), ("causal", C.c_int32), ("v_layout", C.c_int32),
+        ("out_dtype", C.c_int32),
+        ("q_offset", C.c_int64), ("kv_offset", C.c_int64),
+        ("split_keys", C.c_int32), ("max_ctas", C.c_int32),
+    ]
+
+
+_lib = None
+
+
+def lib(path: Path | None = None) -> C.CDLL:
+    """Load libfa8.so (raises OSError if it has not been built)."""
+    global _lib
+    if _lib is None or path is not None:
+        p = Path(path) if path is not None else _build.LIB
+        L = C.CDLL(str(p))
+        L.fa8_fwd_params_init.argtypes = [C.POINTER(Fa8FwdParams)] + [C.c_int64] * 6
+        L.fa8_fwd_params_init.restype = None
+        L.fa8_fwd.argtypes = [C.POINTER(Fa8FwdParams), C.c_void_p]
+        L.fa8_fwd.restype = C.c_int
+        L.fa8_lse_merge.argtypes = [C.c_int, C.POINTER(C.c_void_p), C.c_int,
+                                    C.POINTER(C.c_void_p), C.c_int64, C.c_int64, C.c_void_p,
+                                    C.c_int64, C.c_void_p, C.c_void_p]
+        L.fa8_lse_merge.restype = C.c_int
+        L.fa8_quantize_e4m3.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64,
+                                        C.c_int64, C.c_float, C.c_int, C.c_void_p]
+        L.fa8_quantize_e4m3.restype = C.c_int
+        L.fa8_status_string.argtypes = [C.c_int]
+        L.fa8_status_string.restype = C.c_char_p
+        L.fa8_last_error_message.argtypes = []
+        L.fa8_last_error_message.restype = C.c_char_p
+        L.fa8_launch_count.argtypes = []
+        L.fa8_launch_count.restype = C.c_uint64
+        if path is not None:
+            return L
+        _lib = L
+    return _lib
+
+
+def params(batch, heads, heads_kv, seqlen_q, seqlen_kv, head_dim) -> Fa8FwdParams:
+    p = Fa8FwdParams()
+    lib().fa8_fwd_params_init(C.byref(p), batch, heads, heads_kv, seqlen_q, seqlen_kv, head_dim)
+    return p
+
+
+def check(status: int) -> None:
+    if status != FA8_OK:
+        L = lib()
+        raise RuntimeError(f"fa8 status {status}: {L.fa8_status_string(status).decode()}: "
+                           f"{L.fa8_last_error_message().decode()}")
+
+
+def fwd(p: Fa8FwdParams, stream: int = 0) -> int:
+    return lib().fa8_fwd(C.byref(p), C.c_void_p(stream))
+
+
+def lse_merge(o_ptrs, o_is_f16, lse_ptrs, rows, head_dim, o_out, o_out_stride, lse_out,
+              stream: int = 0) -> int:
+    n = len(o_ptrs)
+    oa = (C.c_void_p * n)(*o_ptrs)
+    la = (C.c_void_p * n)(*lse_ptrs)
+    return lib().fa8_lse_merge(n, oa, int(o_is_f16), la, rows, head_dim, o_out, o_out_stride,
+                               lse_out, C.c_void_p(stream))
+
+
+def quantize_e4m3(x_ptr, in_dtype, y_ptr, batch, rows, cols, scale, transpose,
+                  stream: int = 0) -> int:
+    return lib().fa8_quantize_e4m3(x_ptr, in_dtype, y_ptr, batch, rows, cols, scale,
+                                   int(transpose), C.c_void_p(stream))

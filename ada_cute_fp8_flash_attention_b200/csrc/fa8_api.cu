@@ -1,0 +1,252 @@
+// fa8_api.cu — C-ABI host side of the sm_100a FP8 attention forward.
+//
+// Replaces the reference's host path (csrc/flash_attention.cu:462-543:
+// fill_params, launch_flash_attn_fp8_kernel, flash_attn_fp8_forward) with a
+// status-returning, non-blocking launcher:
+//   * no cudaDeviceSynchronize after the launch (reference :539) and no
+//     exit() on error (reference include/attention_api.cuh:28-37);
+//   * the dynamic shared-memory attribute is set once per device and kernel
+//     instead of on every call (reference :503);
+//   * operands are described to the kernel as TMA tensor maps (4-D:
+//     innermost dim, rows, heads, batch) so ragged sequence ends are
+//     zero-filled by hardware instead of requiring S % 64 == 0 (reference
+//     F7: no load predicates).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/fa8.h"
+#include "fa8_fwd_kernel.cuh"
+
+namespace {
+
+thread_local char g_last_msg[512] = "";
+std::atomic<uint64_t> g_launches{0};
+
+int set_cuda_error(cudaError_t e, const char* where) {
+  snprintf(g_last_msg, sizeof(g_last_msg), "%s: %s", where, cudaGetErrorString(e));
+  return FA8_ERR_CUDA;
+}
+int set_msg(int status, const char* msg) {
+  snprintf(g_last_msg, sizeof(g_last_msg), "%s", msg);
+  return status;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 4-D byte tensor map: dims {inner, rows, heads, batch}, box {box_inner, box_rows, 1, 1}.
+int make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
+                uint64_t heads, uint64_t batch, uint64_t row_stride, uint64_t head_stride,
+                uint64_t batch_stride, uint32_t box_inner, uint32_t box_rows,
+                CUtensorMapSwizzle swz) {
+  auto enc = get_encode_fn();
+  if (!enc) return set_msg(FA8_ERR_DRIVER, "cuTensorMapEncodeTiled entry point not found");
+  cuuint64_t dims[4] = {inner, rows, heads, batch};
+  cuuint64_t strides[3] = {row_stride, head_stride, batch_stride};  // bytes
+  cuuint32_t box[4] = {box_inner, box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    snprintf(g_last_msg, sizeof(g_last_msg), "cuTensorMapEncodeTiled failed (CUresult %d)",
+             (int)r);
+    return FA8_ERR_ALIGNMENT;
+  }
+  return FA8_OK;
+}
+
+template <int D>
+int setup_kernel_attr(int dev) {
+  static std::once_flag flags[64];
+  static cudaError_t errs[64];
+  if (dev < 0 || dev >= 64) return set_msg(FA8_ERR_INVALID_ARG, "device index out of range");
+  std::call_once(flags[dev], [dev] {
+    errs[dev] = cudaFuncSetAttribute(fa8::fa8_fwd_kernel<D>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     fa8::TileCfg<D>::kSmemAlloc);
+  });
+  if (errs[dev] != cudaSuccess) return set_cuda_error(errs[dev], "cudaFuncSetAttribute");
+  return FA8_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int D>
+int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
+  using C = fa8::TileCfg<D>;
+  int st = setup_kernel_attr<D>(dev);
+  if (st) return st;
+  const CUtensorMapSwizzle swz_qk =
+      (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUtensorMap tq, tk, tv;
+  memset(&tk, 0, sizeof(tk));
+  memset(&tv, 0, sizeof(tv));
+  st = make_map_u8(&tq, p->q, D, p->seqlen_q, p->heads, p->batch, p->q_stride_s, p->q_stride_h,
+                   p->q_stride_b, D, fa8::kBlockM, swz_qk);
+  if (st) return st;
+  if (p->seqlen_kv > 0) st = make_map_u8(&tk, p->k, D, p->seqlen_kv, p->heads_kv, p->batch, p->k_stride_s,
+                   p->k_stride_h, p->k_stride_b, D, fa8::kBlockN, swz_qk);
+  if (st) return st;
+  // V^T (BHDS): innermost = keys, rows = d.
+  if (p->seqlen_kv > 0) st = make_map_u8(&tv, p->v, p->seqlen_kv, D, p->heads_kv, p->batch, p->v_stride_r,
+                   p->v_stride_h, p->v_stride_b, fa8::kBlockN, D, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+
+  fa8::KernelParams kp;
+  kp.batch = (int)p->batch;
+  kp.heads = (int)p->heads;
+  kp.heads_kv = (int)p->heads_kv;
+  kp.seqlen_q = (int)p->seqlen_q;
+  kp.seqlen_kv = (int)p->seqlen_kv;
+  kp.head_group = (int)(p->heads / p->heads_kv);
+  kp.causal = p->causal ? 1 : 0;
+  kp.out_e4m3 = p->out_dtype == FA8_OUT_E4M3 ? 1 : 0;
+  kp.split_keys = p->split_keys < 0 ? fa8::kDefaultSplitKeys : p->split_keys;
+  const int rows_per_cta = fa8::kTilesPerCta * fa8::kBlockM;
+  kp.n_qblocks = (int)((p->seqlen_q + rows_per_cta - 1) / rows_per_cta);
+  kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  kp.q_offset = p->q_offset;
+  kp.kv_offset = p->kv_offset;
+  kp.o = p->o;
+  kp.o_sb = p->o_stride_b;
+  kp.o_sh = p->o_stride_h;
+  kp.o_ss = p->o_stride_s;
+  kp.lse = p->lse;
+  kp.lse_sb = p->lse_stride_b;
+  kp.lse_sh = p->lse_stride_h;
+  kp.status = p->status;
+
+  dim3 grid(kp.n_qblocks, (unsigned)p->heads, (unsigned)p->batch);
+  fa8::fa8_fwd_kernel<D><<<grid, fa8::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, kp);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "fa8_fwd_kernel launch");
+  return FA8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void fa8_fwd_params_init(fa8_fwd_params* p, int64_t batch, int64_t heads, int64_t heads_kv,
+                         int64_t seqlen_q, int64_t seqlen_kv, int64_t head_dim) {
+  memset(p, 0, sizeof(*p));
+  p->batch = batch;
+  p->heads = heads;
+  p->heads_kv = heads_kv;
+  p->seqlen_q = seqlen_q;
+  p->seqlen_kv = seqlen_kv;
+  p->head_dim = head_dim;
+  p->q_stride_s = head_dim;
+  p->q_stride_h = seqlen_q * head_dim;
+  p->q_stride_b = heads * seqlen_q * head_dim;
+  p->k_stride_s = head_dim;
+  p->k_stride_h = seqlen_kv * head_dim;
+  p->k_stride_b = heads_kv * seqlen_kv * head_dim;
+  p->v_stride_r = seqlen_kv;  // BHDS: d rows of seqlen_kv keys
+  p->v_stride_h = head_dim * seqlen_kv;
+  p->v_stride_b = heads_kv * head_dim * seqlen_kv;
+  p->o_stride_s = head_dim;
+  p->o_stride_h = seqlen_q * head_dim;
+  p->o_stride_b = heads * seqlen_q * head_dim;
+  p->lse_stride_h = seqlen_q;
+  p->lse_stride_b = heads * seqlen_q;
+  p->softmax_scale = head_dim > 0 ? 1.0f / sqrtf((float)head_dim) : 1.0f;
+  p->causal = 0;
+  p->v_layout = FA8_V_BHDS;
+  p->out_dtype = FA8_OUT_F16;
+  p->split_keys = -1;
+}
+
+int fa8_fwd(const fa8_fwd_params* p, void* stream) {
+  if (!p) return set_msg(FA8_ERR_INVALID_ARG, "params is NULL");
+  if (p->batch < 0 || p->heads < 0 || p->heads_kv < 0 || p->seqlen_q < 0 || p->seqlen_kv < 0)
+    return set_msg(FA8_ERR_INVALID_ARG, "negative size");
+  if (p->head_dim != 64 && p->head_dim != 128)
+    return set_msg(FA8_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (p->v_layout != FA8_V_BHDS)
+    return set_msg(FA8_ERR_UNSUPPORTED, "only the BHDS (pre-transposed) V layout is supported");
+  if (p->out_dtype != FA8_OUT_F16 && p->out_dtype != FA8_OUT_E4M3)
+    return set_msg(FA8_ERR_INVALID_ARG, "out_dtype must be FA8_OUT_F16 or FA8_OUT_E4M3");
+  if (p->batch == 0 || p->heads == 0 || p->seqlen_q == 0) return FA8_OK;
+  if (p->heads_kv <= 0 || p->heads % p->heads_kv != 0)
+    return set_msg(FA8_ERR_UNSUPPORTED, "heads must be a multiple of heads_kv");
+  if (p->batch > 65535 || p->heads > 65535 || p->seqlen_q > (1ll << 30) ||
+      p->seqlen_kv > (1ll << 30))
+    return set_msg(FA8_ERR_UNSUPPORTED, "size exceeds the supported grid / index range");
+  if (!p->q || !p->o || (p->seqlen_kv > 0 && (!p->k || !p->v)))
+    return set_msg(FA8_ERR_INVALID_ARG, "null tensor pointer");
+  if (!(p->softmax_scale > 0.f) || !std::isfinite(p->softmax_scale))
+    return set_msg(FA8_ERR_INVALID_ARG, "softmax_scale must be positive and finite");
+  if (!aligned16(p->q) || !aligned16(p->o) ||
+      (p->seqlen_kv > 0 && (!aligned16(p->k) || !aligned16(p->v))))
+    return set_msg(FA8_ERR_ALIGNMENT, "tensor base addresses must be 16-byte aligned");
+  const int64_t osz = p->out_dtype == FA8_OUT_E4M3 ? 1 : 2;
+  const int64_t s16[] = {p->q_stride_b, p->q_stride_h, p->q_stride_s, p->k_stride_b,
+                         p->k_stride_h, p->k_stride_s, p->v_stride_b, p->v_stride_h,
+                         p->v_stride_r};
+  const int n_checked = p->seqlen_kv > 0 ? 9 : 3;  // no K/V access without keys
+  for (int j = 0; j < n_checked; ++j) {
+    const int64_t s = s16[j];
+    if (s <= 0 || (s % 16) != 0)
+      return set_msg(FA8_ERR_ALIGNMENT,
+                     "Q/K/V strides must be positive multiples of 16 elements (TMA); for BHDS V "
+                     "this means seqlen_kv % 16 == 0");
+  }
+  if ((p->o_stride_s * osz) % 16 || (p->o_stride_h * osz) % 16 || (p->o_stride_b * osz) % 16)
+    return set_msg(FA8_ERR_ALIGNMENT, "O strides must be multiples of 16 bytes");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, "cudaGetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0)
+    return set_msg(FA8_ERR_NO_DEVICE, "the current device is not sm_100 (B200)");
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return p->head_dim == 128 ? launch<128>(p, s, dev) : launch<64>(p, s, dev);
+}
+
+const char* fa8_status_string(int status) {
+  switch (status) {
+    case FA8_OK: return "ok";
+    case FA8_ERR_INVALID_ARG: return "invalid argument";
+    case FA8_ERR_UNSUPPORTED: return "unsupported configuration";
+    case FA8_ERR_ALIGNMENT: return "alignment / stride requirement violated";
+    case FA8_ERR_CUDA: return "CUDA runtime error";
+    case FA8_ERR_DRIVER: return "CUDA driver entry point unavailable";
+    case FA8_ERR_NO_DEVICE: return "no sm_100 device";
+    default: return "unknown status";
+  }
+}
+
+const char* fa8_last_error_message(void) { return g_last_msg; }
+
+uint64_t fa8_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+}  // extern "C"
+
+// Used by the auxiliary kernels' translation unit.
+void fa8_note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+int fa8_note_cuda_error(cudaError_t e, const char* where) { return set_cuda_error(e, where); }
+int fa8_note_error(int status, const char* msg) { return set_msg(status, msg); }

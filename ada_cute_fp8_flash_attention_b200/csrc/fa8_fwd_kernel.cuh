@@ -1,0 +1,567 @@
+// fa8_fwd_kernel.cuh — warp-specialised FP8 (e4m3) flash-attention forward
+// for sm_100a.
+//
+// Replaces the reference's FA2-style Ada kernel flash_attn_fp8_kernel
+// (csrc/flash_attention.cu:90-460) and its traits (csrc/kernel_traits.h:11-87)
+// with a Blackwell design:
+//
+//   * one CTA owns two 128-row query tiles (Q0, Q1) of one (batch, head);
+//   * 384 threads = three warpgroups; warps 10-11 of the control warpgroup
+//     are idle;
+//   * warp 9 (TMA) streams K and V tiles (128 keys each) into a ring of
+//     shared-memory stages (cp.async.bulk.tensor, mbarrier completion);
+//   * warp 8 (one elected thread) issues tcgen05.mma kind::f8f6f4:
+//       S_i = Q_i K^T  into TMEM (128 lanes x 128 f32 columns per tile),
+//       O_i += P_i V   into TMEM (128 lanes x D f32 columns per tile);
+//   * warps 0-3 and 4-7 are the softmax warpgroups of Q0 and Q1. Each thread
+//     owns one query row (one TMEM lane): row max and row sum need no
+//     shuffles. They run the online softmax in base 2 (the reference's
+//     softmax_rescale_o, csrc/flash_attention.cu:54-88, with the scale fixed
+//     to softmax_scale * log2(e)), requantise P to e4m3 into a 128B-swizzled
+//     shared tile for the PV product, rescale O in TMEM only when the row max
+//     grew by more than kRescaleThreshold (lazy rescale), and finally
+//     normalise O by the row sum (the reference's final_softmax_rescale_o,
+//     csrc/flash_attention.cu:38-52) and store it.
+//
+// K/V tiles are visited from the last needed tile down to tile 0 — the same
+// diagonal-first order as the reference's main loop
+// (csrc/flash_attention.cu:345-428) — so for causal attention the masked
+// diagonal tile comes first. The causal mask keeps key_pos <= query_pos as
+// in csrc/flash_attention.cu:292-304 (and test.py:10-12), in global
+// positions (q_offset / kv_offset) so context-parallel chunks mask
+// correctly.
+//
+// Numerics of the P requantisation (the reference casts P in (0,1] straight
+// to e4m3, csrc/flash_attention.cu:312-320):
+//   * P is formed as 2^(s*scale*log2e - m + kPShift) so typical
+//     probabilities sit in e4m3's normal range, not in its subnormals;
+//     with the lazy-rescale threshold the largest P is 2^(kPShift +
+//     kRescaleThreshold) = 256 < 448 (e4m3 max).
+//   * for query tiles whose rows see few keys (short causal prefixes) P is
+//     split as hi = e4m3(P), lo = e4m3(P - hi) and both are multiplied by V,
+//     which brings the relative error of P from 2^-4 to about 2^-8.
+//   * the row sum is accumulated from the unquantised fp32 P.
+//
+// Every mbarrier wait is bounded: after kTimeoutCycles the waiting thread
+// raises a CTA-wide abort flag, ORs FA8_DEVERR_TIMEOUT into the optional
+// status word and all roles leave their loops, drain their in-flight
+// copies / MMAs with bounded waits, free TMEM and exit.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+
+namespace fa8 {
+
+constexpr int kThreads = 384;          // 2 softmax warpgroups + 1 control warpgroup
+constexpr int kBlockM = 128;           // query rows per tile (= TMEM lanes)
+constexpr int kBlockN = 128;           // keys per K/V tile
+constexpr int kTilesPerCta = 2;        // query tiles per CTA
+constexpr int kMmaWarp = 8;
+constexpr int kLoadWarp = 9;
+constexpr float kPShift = 7.0f;        // log2 of the P scale-up
+constexpr float kRescaleThreshold = 1.0f;  // log2 units
+constexpr long long kTimeoutCycles = 4000000000LL;
+constexpr int kDefaultSplitKeys = 1024;
+
+template <int D>
+struct TileCfg {
+  static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
+  static constexpr int kQKRowBytes = D;                  // e4m3 rows of Q and K
+  static constexpr int kQBytes = kBlockM * D;
+  static constexpr int kKBytes = kBlockN * D;
+  static constexpr int kVBytes = D * kBlockN;            // V^T tile: D rows of 128 keys
+  static constexpr int kStageBytes = kKBytes;            // == kVBytes
+  static constexpr int kStages = (D == 128) ? 6 : 8;
+  static constexpr int kPBytes = kBlockM * kBlockN;      // 128 rows x 128 B
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffRing = kTilesPerCta * kQBytes;
+  static constexpr int kOffP = kOffRing + kStages * kStageBytes;
+  static constexpr int kSmemBytes = kOffP + 2 * kTilesPerCta * kPBytes;  // hi + lo per tile
+  static constexpr int kSmemAlloc = kSmemBytes + 1024;   // slack for 1024-B alignment
+  // TMEM columns: S0 | S1 | O0 | O1
+  static constexpr uint32_t kColS = 0;
+  static constexpr uint32_t kColO = kTilesPerCta * kBlockN;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kIdescS = ptx::idesc_e4m3_f32(kBlockM, kBlockN);
+  static constexpr uint32_t kIdescO = ptx::idesc_e4m3_f32(kBlockM, D);
+};
+
+struct KernelParams {
+  int batch, heads, heads_kv, seqlen_q, seqlen_kv, head_group;
+  int causal, out_e4m3, split_keys, n_qblocks;
+  float scale_log2;
+  long long q_offset, kv_offset;
+  void* o;
+  long long o_sb, o_sh, o_ss;
+  float* lse;
+  long long lse_sb, lse_sh;
+  int* status;
+};
+
+// Barrier slots in static shared memory.
+template <int NS>
+struct Bars {
+  uint64_t q_full[kTilesPerCta];
+  uint64_t kv_full[NS];
+  uint64_t kv_empty[NS];
+  uint64_t s_full[kTilesPerCta];
+  uint64_t s_free[kTilesPerCta];
+  uint64_t p_full[kTilesPerCta];
+  uint64_t o_done[kTilesPerCta];
+  uint64_t drain;
+};
+
+// Bounded wait on phase `parity` of `bar`. Returns false on abort/timeout.
+__device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort_flag, int* status) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      *abort_flag = 1;
+      if (status) atomicOr(status, 1);
+      return false;
+    }
+  }
+}
+
+// Number of K/V tiles query tile `i` needs, and whether its P is split.
+struct TilePlan {
+  int n;       // K/V tiles (tile indices 0 .. n-1)
+  int split;   // hi/lo requantisation of P
+  int q_start; // first query row (local)
+};
+
+__device__ __forceinline__ TilePlan plan_tile(const KernelParams& p, int qb, int i) {
+  TilePlan t;
+  t.q_start = qb * (kTilesPerCta * kBlockM) + i * kBlockM;
+  t.n = 0;
+  t.split = 0;
+  if (t.q_start >= p.seqlen_q) return t;
+  const int n_kv = (p.seqlen_kv + kBlockN - 1) / kBlockN;
+  long long visible_first;
+  if (p.causal) {
+    const long long last_row = min(t.q_start + kBlockM - 1, p.seqlen_q - 1);
+    const long long max_key = p.q_offset + last_row - p.kv_offset;  // local key index
+    t.n = max_key < 0 ? 0 : (int)min((long long)n_kv, max_key / kBlockN + 1);
+    visible_first = p.q_offset + t.q_start - p.kv_offset + 1;
+    if (visible_first > p.seqlen_kv) visible_first = p.seqlen_kv;
+  } else {
+    t.n = n_kv;
+    visible_first = p.seqlen_kv;
+  }
+  t.split = (t.n > 0 && visible_first < p.split_keys) ? 1 : 0;
+  return t;
+}
+
+// Write one row of O (fp16 or e4m3) from 32 f32 values at column chunk `c`.
+__device__ __forceinline__ void store_o_chunk(const KernelParams& p, char* row_ptr, int c,
+                                              const float (&v)[32]) {
+  if (!p.out_e4m3) {
+    uint4* dst = reinterpret_cast<uint4*>(row_ptr + c * 32 * 2);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        __half2 h = __floats2half2_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+        w[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+    uint4* dst = reinterpret_cast<uint4*>(row_ptr + c * 32);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int base = 16 * j + 4 * e;
+        w[e] = (uint32_t)ptx::cvt_e4m3x2(v[base], v[base + 1]) |
+               ((uint32_t)ptx::cvt_e4m3x2(v[base + 2], v[base + 3]) << 16);
+      }
+      dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const KernelParams p) {
+  using C = TileCfg<D>;
+  constexpr int NS = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ Bars<NS> bars;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int qb = p.causal ? (p.n_qblocks - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int hk = h / p.head_group;
+
+  TilePlan tp[kTilesPerCta];
+#pragma unroll
+  for (int i = 0; i < kTilesPerCta; ++i) tp[i] = plan_tile(p, qb, i);
+  const int nmax = max(tp[0].n, tp[1].n);
+
+  char* o_head = reinterpret_cast<char*>(p.o) +
+                 ((long long)b * p.o_sb + (long long)h * p.o_sh) * (p.out_e4m3 ? 1 : 2);
+  float* lse_head = p.lse ? p.lse + (long long)b * p.lse_sb + (long long)h * p.lse_sh : nullptr;
+
+  if (nmax == 0) {
+    // Every row of this CTA is fully masked: O = 0, LSE = -inf.
+    if (warp < 8) {
+      const int i = warp / 4;
+      const int row = tp[i].q_start + (threadIdx.x % kBlockM);
+      if (tp[i].q_start < p.seqlen_q && row < p.seqlen_q) {
+        float z[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) z[j] = 0.f;
+        char* row_ptr = o_head + (long long)row * p.o_ss * (p.out_e4m3 ? 1 : 2);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) store_o_chunk(p, row_ptr, c, z);
+        if (lse_head) lse_head[row] = -INFINITY;
+      }
+    }
+    return;
+  }
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t s_base = ptx::smem_u32(smem);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTilesPerCta; ++i) {
+      ptx::mbar_init(&bars.q_full[i], 1);
+      ptx::mbar_init(&bars.s_full[i], 1);
+      ptx::mbar_init(&bars.s_free[i], 4);
+      ptx::mbar_init(&bars.p_full[i], 4);
+      ptx::mbar_init(&bars.o_done[i], 1);
+    }
+    for (int s = 0; s < NS; ++s) {
+      ptx::mbar_init(&bars.kv_full[s], 1);
+      ptx::mbar_init(&bars.kv_empty[s], 1);
+    }
+    ptx::mbar_init(&bars.drain, 1);
+    abort_sh = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == kMmaWarp) {
+    ptx::tmem_alloc(&tmem_base_sh, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  volatile int* abort_flag = &abort_sh;
+
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      ptx::tma_prefetch_desc(&tm_q);
+      ptx::tma_prefetch_desc(&tm_k);
+      ptx::tma_prefetch_desc(&tm_v);
+      const uint64_t pol_q = ptx::policy_evict_first();
+      const uint64_t pol_kv = ptx::policy_evict_last();
+      for (int i = 0; i < kTilesPerCta; ++i) {
+        if (tp[i].n == 0) continue;
+        ptx::mbar_arrive_expect_tx(&bars.q_full[i], C::kQBytes);
+        ptx::tma_load_4d(smem + C::kOffQ + i * C::kQBytes, &tm_q, &bars.q_full[i], 0,
+                         tp[i].q_start, h, b, pol_q);
+      }
+      int issued = 0;
+      bool ok = true;
+      for (int t = 0; t < nmax && ok; ++t) {
+        const int kv = nmax - 1 - t;
+        for (int part = 0; part < 2 && ok; ++part) {
+          const int L = 2 * t + part;
+          const int st = L % NS;
+          if (L >= NS) ok = bounded_wait(&bars.kv_empty[st], ((L / NS) - 1) & 1, abort_flag, p.status);
+          if (!ok) break;
+          ptx::mbar_arrive_expect_tx(&bars.kv_full[st], C::kStageBytes);
+          uint8_t* dst = smem + C::kOffRing + st * C::kStageBytes;
+          if (part == 0)
+            ptx::tma_load_4d(dst, &tm_k, &bars.kv_full[st], 0, kv * kBlockN, hk, b, pol_kv);
+          else
+            ptx::tma_load_4d(dst, &tm_v, &bars.kv_full[st], kv * kBlockN, 0, hk, b, pol_kv);
+          ++issued;
+        }
+      }
+      if (!ok) {
+        // Drain: wait (bounded) for the last copies issued so that no TMA
+        // write lands in shared memory after this CTA exits.
+        for (int L = max(0, issued - NS); L < issued; ++L) {
+          const long long t0 = clock64();
+          while (!ptx::mbar_try_wait(&bars.kv_full[L % NS], (L / NS) & 1) &&
+                 clock64() - t0 < kTimeoutCycles) {
+          }
+        }
+        for (int i = 0; i < kTilesPerCta; ++i) {
+          if (tp[i].n == 0) continue;
+          const long long t0 = clock64();
+          while (!ptx::mbar_try_wait(&bars.q_full[i], 0) && clock64() - t0 < kTimeoutCycles) {
+          }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t q_addr[2] = {s_base + C::kOffQ, s_base + C::kOffQ + C::kQBytes};
+      const uint32_t p_hi[2] = {s_base + C::kOffP, s_base + C::kOffP + C::kPBytes};
+      const uint32_t p_lo[2] = {s_base + C::kOffP + 2 * C::kPBytes,
+                                s_base + C::kOffP + 3 * C::kPBytes};
+      const int start[2] = {nmax - tp[0].n, nmax - tp[1].n};
+      bool ok = true;
+      for (int i = 0; i < kTilesPerCta && ok; ++i)
+        if (tp[i].n > 0) ok = bounded_wait(&bars.q_full[i], 0, abort_flag, p.status);
+      for (int t = -1; t < nmax && ok; ++t) {
+        // S_i(t+1) = Q_i K(t+1)^T
+        if (t + 1 < nmax) {
+          const int L = 2 * (t + 1);
+          const int st = L % NS;
+          ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
+          if (!ok) break;
+          const uint32_t k_addr = s_base + C::kOffRing + st * C::kStageBytes;
+          for (int i = 0; i < kTilesPerCta; ++i) {
+            const int tl = t + 1 - start[i];
+            if (tp[i].n == 0 || tl < 0) continue;
+            if (tl > 0) {
+              ok = bounded_wait(&bars.s_free[i], (tl - 1) & 1, abort_flag, p.status);
+              if (!ok) break;
+            }
+            ptx::tc_fence_after();
+            const uint32_t d_tmem = tmem + C::kColS + i * kBlockN;
+#pragma unroll
+            for (int kk = 0; kk < D / 32; ++kk) {
+              ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(q_addr[i] + kk * 32, C::kQKRowBytes),
+                           ptx::smem_desc_kmajor(k_addr + kk * 32, C::kQKRowBytes), C::kIdescS,
+                           kk > 0 ? 1u : 0u);
+            }
+            ptx::umma_commit(&bars.s_full[i]);
+          }
+          if (!ok) break;
+          ptx::umma_commit(&bars.kv_empty[st]);
+        }
+        // O_i += P_i(t) V(t)
+        if (t >= 0) {
+          const int L = 2 * t + 1;
+          const int st = L % NS;
+          ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
+          if (!ok) break;
+          const uint32_t v_addr = s_base + C::kOffRing + st * C::kStageBytes;
+          for (int i = 0; i < kTilesPerCta; ++i) {
+            const int tl = t - start[i];
+            if (tp[i].n == 0 || tl < 0) continue;
+            ok = bounded_wait(&bars.p_full[i], tl & 1, abort_flag, p.status);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            const uint32_t d_tmem = tmem + C::kColO + i * D;
+#pragma unroll
+            for (int kk = 0; kk < kBlockN / 32; ++kk) {
+              ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_hi[i] + kk * 32, 128),
+                           ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO,
+                           (tl > 0 || kk > 0) ? 1u : 0u);
+            }
+            if (tp[i].split) {
+#pragma unroll
+              for (int kk = 0; kk < kBlockN / 32; ++kk) {
+                ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_lo[i] + kk * 32, 128),
+                             ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO, 1u);
+              }
+            }
+            ptx::umma_commit(&bars.o_done[i]);
+          }
+          if (!ok) break;
+          ptx::umma_commit(&bars.kv_empty[st]);
+        }
+      }
+      // Drain every MMA issued before TMEM is freed.
+      ptx::umma_commit(&bars.drain);
+      const long long t0 = clock64();
+      while (!ptx::mbar_try_wait(&bars.drain, 0) && clock64() - t0 < kTimeoutCycles) {
+      }
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ softmax WGs
+    const int i = warp / 4;                 // query tile of this warpgroup
+    const int r = threadIdx.x % kBlockM;    // row within the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + C::kColS + i * kBlockN;
+    const uint32_t t_o = tmem + lane_off + C::kColO + i * D;
+    const uint32_t p_hi = s_base + C::kOffP + i * C::kPBytes;
+    const uint32_t p_lo = s_base + C::kOffP + (2 + i) * C::kPBytes;
+    const int n = tp[i].n;
+    const int row = tp[i].q_start + r;  // local query row
+    const long long row_g = p.q_offset + row;
+    const float sl2 = p.scale_log2;
+    float m_run = -INFINITY;  // running max of s*scale*log2e
+    float l_run = 0.f;
+    bool ok = true;
+
+    for (int tl = 0; tl < n && ok; ++tl) {
+      const int kv = n - 1 - tl;
+      ok = bounded_wait(&bars.s_full[i], tl & 1, abort_flag, p.status);
+      if (!ok) break;
+      ptx::tc_fence_after();
+      float s[kBlockN];
+      {
+        uint32_t u[kBlockN / 32][32];
+#pragma unroll
+        for (int c = 0; c < kBlockN / 32; ++c) ptx::tmem_ld32(t_s + c * 32, u[c]);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < kBlockN / 32; ++c) {
+          ptx::reg_fence32(u[c]);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(u[c][j]);
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars.s_free[i]);
+
+      // Mask: keys past seqlen_kv, and (causal) keys after this query.
+      const int kv0 = kv * kBlockN;
+      long long lim = p.seqlen_kv - kv0;
+      if (p.causal) lim = min(lim, row_g - p.kv_offset - kv0 + 1);
+      if (lim < kBlockN) {
+        const int li = (int)max(lim, -1LL);
+#pragma unroll
+        for (int c = 0; c < kBlockN; ++c)
+          if (c >= li) s[c] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < kBlockN; ++c) mx = fmaxf(mx, s[c]);
+      const float m_tile = mx * sl2;
+      const float m_new = fmaxf(m_run, m_tile);
+      const bool need = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold || tl == 0);
+      const float m_use = need ? m_new : m_run;
+      const float base = (m_use == -INFINITY) ? 0.f : (m_use - kPShift);
+      float alpha = 1.f;
+      if (need) alpha = (m_run == -INFINITY) ? 0.f : ptx::ex2(m_run - m_use);
+      m_run = m_use;
+
+      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBlockN; c += 4) {
+        s[c + 0] = ptx::ex2(fmaf(s[c + 0], sl2, -base));
+        s[c + 1] = ptx::ex2(fmaf(s[c + 1], sl2, -base));
+        s[c + 2] = ptx::ex2(fmaf(s[c + 2], sl2, -base));
+        s[c + 3] = ptx::ex2(fmaf(s[c + 3], sl2, -base));
+        sum0 += s[c + 0];
+        sum1 += s[c + 1];
+        sum2 += s[c + 2];
+        sum3 += s[c + 3];
+      }
+      l_run = l_run * alpha + ((sum0 + sum1) + (sum2 + sum3));
+
+      // e4m3 P (hi) and, for split tiles, the e4m3 residual P - hi (lo).
+      uint32_t ph[kBlockN / 4];
+      uint32_t pl[kBlockN / 4];
+      const bool split = tp[i].split != 0;
+#pragma unroll
+      for (int j = 0; j < kBlockN / 4; ++j) {
+        ph[j] = (uint32_t)ptx::cvt_e4m3x2(s[4 * j], s[4 * j + 1]) |
+                ((uint32_t)ptx::cvt_e4m3x2(s[4 * j + 2], s[4 * j + 3]) << 16);
+        if (split) {
+          const uint32_t h01 = ptx::cvt_e4m3x2_to_f16x2((uint16_t)(ph[j] & 0xffffu));
+          const uint32_t h23 = ptx::cvt_e4m3x2_to_f16x2((uint16_t)(ph[j] >> 16));
+          const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+          const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+          pl[j] = (uint32_t)ptx::cvt_e4m3x2(s[4 * j] - f01.x, s[4 * j + 1] - f01.y) |
+                  ((uint32_t)ptx::cvt_e4m3x2(s[4 * j + 2] - f23.x, s[4 * j + 3] - f23.y) << 16);
+        } else {
+          pl[j] = 0u;
+        }
+      }
+
+      // PV(t-1) must be complete before O is rescaled or P overwritten.
+      if (tl > 0) {
+        ok = bounded_wait(&bars.o_done[i], (tl - 1) & 1, abort_flag, p.status);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        if (need) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t u[32];
+            ptx::tmem_ld32(t_o + c * 32, u);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence32(u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(__uint_as_float(u[j]) * alpha);
+            ptx::tmem_st32(t_o + c * 32, u);
+          }
+          ptx::tmem_wait_st();
+        }
+      }
+      const uint32_t row_addr_hi = p_hi + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        ptx::st_shared_v4(row_addr_hi + ((c ^ (r & 7)) << 4), ph[4 * c], ph[4 * c + 1],
+                          ph[4 * c + 2], ph[4 * c + 3]);
+      if (split) {
+        const uint32_t row_addr_lo = p_lo + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          ptx::st_shared_v4(row_addr_lo + ((c ^ (r & 7)) << 4), pl[4 * c], pl[4 * c + 1],
+                            pl[4 * c + 2], pl[4 * c + 3]);
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars.p_full[i]);
+    }
+
+    // Epilogue: O / l -> global, LSE.
+    if (n > 0 && ok) ok = bounded_wait(&bars.o_done[i], (n - 1) & 1, abort_flag, p.status);
+    if (tp[i].q_start < p.seqlen_q) {
+      ptx::tc_fence_after();
+      const float inv_l = (l_run > 0.f && ok) ? 1.f / l_run : 0.f;
+      char* row_ptr = o_head + (long long)row * p.o_ss * (p.out_e4m3 ? 1 : 2);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        if (n > 0) {
+          uint32_t u[32];
+          ptx::tmem_ld32(t_o + c * 32, u);
+          ptx::tmem_wait_ld();
+          ptx::reg_fence32(u);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(u[j]) * inv_l;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        if (row < p.seqlen_q) store_o_chunk(p, row_ptr, c, v);
+      }
+      if (lse_head && row < p.seqlen_q) {
+        const float base = m_run - kPShift;
+        lse_head[row] =
+            (l_run > 0.f) ? (__log2f(l_run) + base) * 0.69314718055994531f : -INFINITY;
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+}  // namespace fa8

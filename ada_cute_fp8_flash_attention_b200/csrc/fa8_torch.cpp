@@ -1,0 +1,241 @@
+// fa8_torch.cpp — PyTorch-facing host layer above the C ABI (include/fa8.h).
+//
+// Mirrors the reference's extension module (csrc/attention_api.cpp:6-9,
+// include/attention_api.h:9-10): the function `flash_attn_fp8_forward(q, k,
+// v)` with e4m3 Q/K (B, H, S, D) and V pre-transposed to (B, H, D, S)
+// (test.py:51-52). Like the reference it is causal with scale 1/sqrt(D)
+// (csrc/flash_attention.cu:524, :292-304); unlike it, it returns fp16 O
+// (the reference returns e4m3, :526), never blocks on the device (:539) and
+// never exits the process. Input errors raise RuntimeError through
+// TORCH_CHECK as in include/attention_api.cuh:20-26, with dtype / shape
+// checks the reference lacks.
+//
+// flash_attn_fp8_forward_ex adds: non-causal mode, an explicit scale,
+// V in BHSD layout, LSE output, e4m3 output, context-parallel offsets, the
+// P-split threshold and caller-provided output buffers.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "fa8.h"
+
+namespace {
+
+void check_status(int st, const char* what) {
+  TORCH_CHECK(st == FA8_OK, what, " failed: ", fa8_status_string(st), " (",
+              fa8_last_error_message(), ")");
+}
+
+void check_fp8_input(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.device().is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::ScalarType::Float8_e4m3fn, name,
+              " must be torch.float8_e4m3fn, got ", t.scalar_type());
+  TORCH_CHECK(t.dim() == 4, name, " must be 4-D, got ", t.dim(), " dims");
+  TORCH_CHECK(t.stride(3) == 1 || t.size(3) == 1, name, " must have a unit-stride last dim");
+}
+
+bool tma_ok(const torch::Tensor& t) {
+  if (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) return false;
+  for (int d = 0; d < 3; ++d)
+    if (t.size(d) > 1 && (t.stride(d) % 16 != 0)) return false;
+  return true;
+}
+
+std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                        bool causal, double softmax_scale,
+                                        const std::string& v_layout, bool return_lse,
+                                        const std::string& out_dtype, int64_t q_offset,
+                                        int64_t kv_offset, int64_t split_keys,
+                                        c10::optional<torch::Tensor> out_opt,
+                                        c10::optional<torch::Tensor> lse_opt) {
+  check_fp8_input(q, "q");
+  check_fp8_input(k, "k");
+  check_fp8_input(v, "v");
+  TORCH_CHECK(k.device() == q.device() && v.device() == q.device(),
+              "q, k, v must be on the same device");
+  TORCH_CHECK(v_layout == "bhds" || v_layout == "bhsd", "v_layout must be 'bhds' or 'bhsd'");
+  TORCH_CHECK(out_dtype == "fp16" || out_dtype == "e4m3", "out_dtype must be 'fp16' or 'e4m3'");
+  const int64_t B = q.size(0), H = q.size(1), Sq = q.size(2), D = q.size(3);
+  const int64_t Hkv = k.size(1), Skv = k.size(2);
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128, got ", D);
+  TORCH_CHECK(k.size(0) == B && k.size(3) == D, "k must be (B, H_kv, S_kv, D)");
+  TORCH_CHECK(Hkv > 0 && H % Hkv == 0, "H must be a multiple of H_kv");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream(q.get_device());
+
+  // V as (B, H_kv, D, S_pad) with S_pad % 16 == 0 (TMA row stride rule).
+  torch::Tensor vt;
+  if (v_layout == "bhds") {
+    TORCH_CHECK(v.size(0) == B && v.size(1) == Hkv && v.size(2) == D && v.size(3) == Skv,
+                "v (bhds) must be (B, H_kv, D, S_kv)");
+    vt = v;
+  } else {
+    TORCH_CHECK(v.size(0) == B && v.size(1) == Hkv && v.size(2) == Skv && v.size(3) == D,
+                "v (bhsd) must be (B, H_kv, S_kv, D)");
+    vt = v.transpose(2, 3);
+  }
+  if (Skv % 16 != 0 || !tma_ok(vt) || vt.stride(3) != 1) {
+    const int64_t Sp = (Skv + 15) / 16 * 16;
+    auto vp = torch::zeros({B, Hkv, D, Sp}, vt.options());
+    vp.narrow(3, 0, Skv).copy_(vt);
+    vt = vp;
+  }
+  if (!tma_ok(q)) q = q.contiguous();
+  if (!tma_ok(k)) k = k.contiguous();
+
+  const bool e4m3_out = out_dtype == "e4m3";
+  torch::Tensor out;
+  if (out_opt.has_value()) {
+    out = *out_opt;
+    TORCH_CHECK(out.device() == q.device(), "out must be on q's device");
+    TORCH_CHECK(out.scalar_type() ==
+                    (e4m3_out ? at::ScalarType::Float8_e4m3fn : at::ScalarType::Half),
+                "out has the wrong dtype");
+    TORCH_CHECK(out.dim() == 4 && out.size(0) == B && out.size(1) == H && out.size(2) == Sq &&
+                    out.size(3) == D && out.stride(3) == 1,
+                "out must be (B, H, S_q, D) with unit last stride");
+  } else {
+    out = torch::empty({B, H, Sq, D},
+                       q.options().dtype(e4m3_out ? at::ScalarType::Float8_e4m3fn
+                                                  : at::ScalarType::Half));
+  }
+  torch::Tensor lse;
+  if (return_lse || lse_opt.has_value()) {
+    if (lse_opt.has_value()) {
+      lse = *lse_opt;
+      TORCH_CHECK(lse.scalar_type() == at::ScalarType::Float && lse.dim() == 3 &&
+                      lse.size(0) == B && lse.size(1) == H && lse.size(2) == Sq &&
+                      lse.stride(2) == 1,
+                  "lse must be float32 (B, H, S_q) with unit last stride");
+    } else {
+      lse = torch::empty({B, H, Sq}, q.options().dtype(at::ScalarType::Float));
+    }
+  }
+
+  fa8_fwd_params p;
+  fa8_fwd_params_init(&p, B, H, Hkv, Sq, Skv, D);
+  p.q = q.data_ptr();
+  p.k = k.data_ptr();
+  p.v = vt.data_ptr();
+  p.o = out.data_ptr();
+  p.lse = lse.defined() ? lse.data_ptr<float>() : nullptr;
+  p.q_stride_b = q.stride(0);
+  p.q_stride_h = q.stride(1);
+  p.q_stride_s = q.stride(2);
+  p.k_stride_b = k.stride(0);
+  p.k_stride_h = k.stride(1);
+  p.k_stride_s = k.stride(2);
+  p.v_stride_b = vt.stride(0);
+  p.v_stride_h = vt.stride(1);
+  p.v_stride_r = vt.stride(2);
+  p.o_stride_b = out.stride(0);
+  p.o_stride_h = out.stride(1);
+  p.o_stride_s = out.stride(2);
+  if (lse.defined()) {
+    p.lse_stride_b = lse.stride(0);
+    p.lse_stride_h = lse.stride(1);
+  }
+  p.softmax_scale = static_cast<float>(softmax_scale);
+  p.causal = causal ? 1 : 0;
+  p.out_dtype = e4m3_out ? FA8_OUT_E4M3 : FA8_OUT_F16;
+  p.q_offset = q_offset;
+  p.kv_offset = kv_offset;
+  p.split_keys = static_cast<int32_t>(split_keys);
+  check_status(fa8_fwd(&p, stream.stream()), "fa8_fwd");
+  if (lse.defined()) return {out, lse};
+  return {out};
+}
+
+}  // namespace
+
+torch::Tensor flash_attn_fp8_forward(torch::Tensor q, torch::Tensor k, torch::Tensor v) {
+  TORCH_CHECK(q.dim() == 4, "q must be (B, H, S, D)");
+  const double scale = 1.0 / std::sqrt(static_cast<double>(q.size(3)));
+  return forward_impl(q, k, v, /*causal=*/true, scale, "bhds", false, "fp16", 0, 0, -1,
+                      c10::nullopt, c10::nullopt)[0];
+}
+
+std::vector<torch::Tensor> flash_attn_fp8_forward_ex(
+    torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal,
+    c10::optional<double> softmax_scale, std::string v_layout, bool return_lse,
+    std::string out_dtype, int64_t q_offset, int64_t kv_offset, int64_t split_keys,
+    c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> lse) {
+  TORCH_CHECK(q.dim() == 4, "q must be (B, H, S, D)");
+  const double scale = softmax_scale.has_value()
+                           ? *softmax_scale
+                           : 1.0 / std::sqrt(static_cast<double>(q.size(3)));
+  return forward_impl(q, k, v, causal, scale, v_layout, return_lse, out_dtype, q_offset,
+                      kv_offset, split_keys, out, lse);
+}
+
+std::vector<torch::Tensor> lse_merge(std::vector<torch::Tensor> outs,
+                                     std::vector<torch::Tensor> lses) {
+  TORCH_CHECK(!outs.empty() && outs.size() == lses.size() && outs.size() <= 16,
+              "lse_merge takes 1..16 (out, lse) pairs");
+  const auto& o0 = outs[0];
+  TORCH_CHECK(o0.device().is_cuda(), "outs must be CUDA tensors");
+  const bool f16 = o0.scalar_type() == at::ScalarType::Half;
+  TORCH_CHECK(f16 || o0.scalar_type() == at::ScalarType::Float, "outs must be fp16 or fp32");
+  const int64_t D = o0.size(-1);
+  const int64_t rows = o0.numel() / D;
+  std::vector<const void*> op;
+  std::vector<const float*> lp;
+  for (size_t i = 0; i < outs.size(); ++i) {
+    TORCH_CHECK(outs[i].is_contiguous() && outs[i].sizes() == o0.sizes() &&
+                    outs[i].scalar_type() == o0.scalar_type() && outs[i].device() == o0.device(),
+                "all outs must be contiguous with one shape / dtype / device");
+    TORCH_CHECK(lses[i].is_contiguous() && lses[i].scalar_type() == at::ScalarType::Float &&
+                    lses[i].numel() == rows,
+                "lse parts must be contiguous float32 with one entry per row");
+    op.push_back(outs[i].data_ptr());
+    lp.push_back(lses[i].data_ptr<float>());
+  }
+  c10::cuda::CUDAGuard guard(o0.device());
+  auto out = torch::empty(o0.sizes(), o0.options().dtype(at::ScalarType::Half));
+  auto lse = torch::empty(lses[0].sizes(), lses[0].options());
+  check_status(fa8_lse_merge((int)outs.size(), op.data(), f16 ? 1 : 0, lp.data(), rows, D,
+                             out.data_ptr(), D, lse.data_ptr<float>(),
+                             at::cuda::getCurrentCUDAStream(o0.get_device()).stream()),
+               "fa8_lse_merge");
+  return {out, lse};
+}
+
+torch::Tensor quantize_e4m3(torch::Tensor x, double scale, bool transpose_last2) {
+  TORCH_CHECK(x.device().is_cuda() && x.is_contiguous(), "x must be a contiguous CUDA tensor");
+  TORCH_CHECK(x.scalar_type() == at::ScalarType::Half || x.scalar_type() == at::ScalarType::BFloat16,
+              "x must be fp16 or bf16");
+  TORCH_CHECK(x.dim() >= 2, "x must have at least 2 dims");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t rows = x.size(-2), cols = x.size(-1);
+  const int64_t batch = rows * cols == 0 ? 0 : x.numel() / (rows * cols);
+  auto sizes = x.sizes().vec();
+  if (transpose_last2) std::swap(sizes[sizes.size() - 1], sizes[sizes.size() - 2]);
+  auto y = torch::empty(sizes, x.options().dtype(at::ScalarType::Float8_e4m3fn));
+  check_status(fa8_quantize_e4m3(x.data_ptr(), x.scalar_type() == at::ScalarType::Half ? 0 : 1,
+                                 y.data_ptr(), batch, rows, cols, (float)scale,
+                                 transpose_last2 ? 1 : 0,
+                                 at::cuda::getCurrentCUDAStream(x.get_device()).stream()),
+               "fa8_quantize_e4m3");
+  return y;
+}
+
+int64_t launch_count() { return (int64_t)fa8_launch_count(); }
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("flash_attn_fp8_forward", &flash_attn_fp8_forward,
+        "FP8 (e4m3) causal flash-attention forward on sm_100a; V in (B,H,D,S); returns fp16 O");
+  m.def("flash_attn_fp8_forward_ex", &flash_attn_fp8_forward_ex, py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("causal") = true, py::arg("softmax_scale") = py::none(),
+        py::arg("v_layout") = "bhds", py::arg("return_lse") = false,
+        py::arg("out_dtype") = "fp16", py::arg("q_offset") = 0, py::arg("kv_offset") = 0,
+        py::arg("split_keys") = -1, py::arg("out") = py::none(), py::arg("lse") = py::none(),
+        "FP8 attention forward with options; returns [out] or [out, lse]");
+  m.def("lse_merge", &lse_merge, "log-sum-exp merge of partial attention outputs");
+  m.def("quantize_e4m3", &quantize_e4m3, py::arg("x"), py::arg("scale") = 1.0,
+        py::arg("transpose_last2") = false, "fp16/bf16 -> e4m3 (optionally transposed)");
+  m.def("launch_count", &launch_count, "kernel launches issued by the C ABI so far");
+}

@@ -1,0 +1,144 @@
+/*
+ * fa8.h — C ABI of the B200 (sm_100a) FP8 flash-attention forward.
+ *
+ * Plain C: pointers, sizes and status codes only. No torch or CUDA types
+ * appear in any signature (streams are passed as `void*` holding a
+ * cudaStream_t). Every entry point returns an fa8_status and never exits
+ * the process or synchronises the device.
+ *
+ * Reference interface replaced (Lemon7-UP/ada_cute_fp8_flash_attention):
+ *   fa8_fwd        <- flash_attn_fp8_forward(q, k, v)
+ *                     csrc/flash_attention.cu:508-543 (host forward),
+ *                     csrc/flash_attention.cu:462-485 (fill_params),
+ *                     csrc/flash_attention.cu:487-506 (launcher),
+ *                     csrc/flash.h:11-26 (Flash_fwd_params),
+ *                     bound at csrc/attention_api.cpp:6-9.
+ *   fa8_lse_merge  <- no counterpart in the reference (which emits no LSE);
+ *                     merges partial outputs of the context-parallel ring.
+ *   fa8_quantize_e4m3 <- the torch casts that prepare the kernel inputs in
+ *                     test.py:35-37 and the V transpose at test.py:51-52.
+ */
+#ifndef FA8_H_
+#define FA8_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum fa8_status {
+  FA8_OK = 0,
+  FA8_ERR_INVALID_ARG = 1,   /* null pointer, negative size, bad layout code  */
+  FA8_ERR_UNSUPPORTED = 2,   /* head_dim not 64/128, heads % heads_kv != 0    */
+  FA8_ERR_ALIGNMENT = 3,     /* TMA needs 16-byte aligned bases and strides   */
+  FA8_ERR_CUDA = 4,          /* a CUDA runtime call failed (see message)      */
+  FA8_ERR_DRIVER = 5,        /* driver entry point for tensor maps missing    */
+  FA8_ERR_NO_DEVICE = 6      /* current device is not sm_100                  */
+} fa8_status;
+
+/* Layout of V. The reference takes V pre-transposed to (B, H_kv, D, S_kv)
+ * (test.py:51-52, csrc/flash_attention.cu:145-148). */
+enum { FA8_V_BHDS = 0, FA8_V_BHSD = 1 };
+
+/* Output element type. fp16 is the north-star contract; e4m3 reproduces the
+ * reference's `empty_like(q)` output (csrc/flash_attention.cu:526). */
+enum { FA8_OUT_F16 = 0, FA8_OUT_E4M3 = 1 };
+
+/* Bits the kernel ORs into *status when a bounded wait gives up. */
+enum { FA8_DEVERR_TIMEOUT = 1 };
+
+/*
+ * All strides are in ELEMENTS. Tensors are indexed [b][h][s][d] for Q, K and
+ * O, [b][h][d][s] for V in FA8_V_BHDS layout. The innermost dimension (d for
+ * Q/K/O, s for V-BHDS) must have unit stride. Q/K/V are e4m3 (1 byte),
+ * O is fp16 or e4m3, LSE is fp32 [b][h][s] (natural log), optional.
+ */
+typedef struct fa8_fwd_params {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;               /* may be NULL */
+  int32_t* status;          /* optional device word; kernel ORs FA8_DEVERR_* */
+
+  int64_t batch;
+  int64_t heads;            /* query heads                                  */
+  int64_t heads_kv;         /* key/value heads, divides heads (GQA)         */
+  int64_t seqlen_q;
+  int64_t seqlen_kv;
+  int64_t head_dim;         /* 64 or 128                                    */
+
+  int64_t q_stride_b, q_stride_h, q_stride_s;
+  int64_t k_stride_b, k_stride_h, k_stride_s;
+  int64_t v_stride_b, v_stride_h, v_stride_r;  /* r = d (BHDS) or s (BHSD)  */
+  int64_t o_stride_b, o_stride_h, o_stride_s;
+  int64_t lse_stride_b, lse_stride_h;          /* s stride is 1             */
+
+  float softmax_scale;      /* natural-log scale, usually 1/sqrt(head_dim)  */
+  int32_t causal;           /* mask key_pos > query_pos                     */
+  int32_t v_layout;         /* FA8_V_BHDS                                   */
+  int32_t out_dtype;        /* FA8_OUT_F16 or FA8_OUT_E4M3                  */
+
+  /* Global positions of row 0 of this Q block and of this K/V block. Only
+   * the causal mask reads them (context-parallel chunks); 0 otherwise. */
+  int64_t q_offset;
+  int64_t kv_offset;
+
+  /* P is requantised to e4m3 as hi + lo (two PV products) for query tiles
+   * whose first row sees fewer than this many keys; -1 selects the default
+   * (1024), 0 disables the split. */
+  int32_t split_keys;
+  /* Upper bound on resident CTAs (0 = all SMs). */
+  int32_t max_ctas;
+} fa8_fwd_params;
+
+/* Fill *p with defaults: contiguous strides for the given shape, scale
+ * 1/sqrt(head_dim), non-causal, BHDS V, fp16 out, default split. */
+void fa8_fwd_params_init(fa8_fwd_params* p, int64_t batch, int64_t heads,
+                         int64_t heads_kv, int64_t seqlen_q, int64_t seqlen_kv,
+                         int64_t head_dim);
+
+/* Launch the forward on `stream` (a cudaStream_t, NULL = legacy default).
+ * Asynchronous; returns after the launch is queued. */
+int fa8_fwd(const fa8_fwd_params* p, void* stream);
+
+/*
+ * Log-sum-exp merge of `n_parts` partial attention outputs of the same rows:
+ *   lse = log(sum_i exp(lse_i)), o = sum_i exp(lse_i - lse) * o_i.
+ * o_parts: n_parts pointers to fp32 [rows][head_dim] or fp16 (o_is_f16);
+ * lse_parts: n_parts pointers to fp32 [rows]. Parts with lse = -inf are
+ * ignored. Writes o_out (fp16 [rows][head_dim], row stride o_out_stride) and
+ * lse_out (fp32, may be NULL). All pointers are device pointers; the two
+ * pointer arrays are host arrays of at most 16 entries.
+ */
+int fa8_lse_merge(int n_parts, const void* const* o_parts, int o_is_f16,
+                  const float* const* lse_parts, int64_t rows,
+                  int64_t head_dim, void* o_out, int64_t o_out_stride,
+                  float* lse_out, void* stream);
+
+/*
+ * Quantise fp16 or bf16 x[rows][cols] (row stride in elements) to e4m3 with
+ * round-to-nearest-even and saturation to +-448, multiplying by `scale`
+ * first. If `transpose` is set, y is written as [cols][rows] per matrix of
+ * `rows` rows (batch = number of matrices, each rows x cols) — the V
+ * transpose to BHDS. in_dtype: 0 = fp16, 1 = bf16.
+ */
+int fa8_quantize_e4m3(const void* x, int in_dtype, void* y, int64_t batch,
+                      int64_t rows, int64_t cols, float scale, int transpose,
+                      void* stream);
+
+/* Human-readable text for an fa8_status, plus the last CUDA error seen by
+ * this thread when the status is FA8_ERR_CUDA. */
+const char* fa8_status_string(int status);
+const char* fa8_last_error_message(void);
+
+/* Number of kernel launches fa8_* entry points issued from this process. */
+uint64_t fa8_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA8_H_ */
