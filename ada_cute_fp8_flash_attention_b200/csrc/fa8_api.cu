@@ -246,6 +246,15 @@ uint64_t fa8_launch_count(void) { return g_launches.load(std::memory_order_relax
 
 }  // extern "C"
 
+#ifdef FA8_TRACE
+extern "C" int fa8_trace_fetch(long long* host_buf) {
+  return cudaMemcpyFromSymbol(host_buf, fa8::fa8_trace_buf, sizeof(fa8::fa8_trace_buf)) ==
+                 cudaSuccess
+             ? 0
+             : 1;
+}
+#endif
+
 // Used by the auxiliary kernels' translation unit.
 void fa8_note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 int fa8_note_cuda_error(cudaError_t e, const char* where) { return set_cuda_error(e, where); }

@@ -61,8 +61,8 @@ constexpr int kBlockN = 128;           // keys per K/V tile
 constexpr int kTilesPerCta = 2;        // query tiles per CTA
 constexpr int kMmaWarp = 8;
 constexpr int kLoadWarp = 9;
-constexpr float kPShift = 7.0f;        // log2 of the P scale-up
-constexpr float kRescaleThreshold = 1.0f;  // log2 units
+constexpr float kPShift = 6.0f;        // log2 of the P scale-up
+constexpr float kRescaleThreshold = 2.0f;  // log2 units
 constexpr long long kTimeoutCycles = 4000000000LL;
 constexpr int kDefaultSplitKeys = 1024;
 
@@ -101,6 +101,21 @@ struct KernelParams {
   int* status;
 };
 
+#ifdef FA8_TRACE
+// Debug-only phase timestamps (clock64) of CTA (0,0,0): [role][step][event].
+// role 0/1 = softmax warpgroup 0/1 (thread 0 of the group), role 2 = MMA thread.
+__device__ long long fa8_trace_buf[3][64][8];
+#define FA8_TR(role, step, ev)                                                 \
+  do {                                                                         \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (step) < 64)  \
+      fa8_trace_buf[role][step][ev] = clock64();                               \
+  } while (0)
+#else
+#define FA8_TR(role, step, ev) \
+  do {                         \
+  } while (0)
+#endif
+
 // Barrier slots in static shared memory.
 template <int NS>
 struct Bars {
@@ -117,10 +132,14 @@ struct Bars {
 // Bounded wait on phase `parity` of `bar`. Returns false on abort/timeout.
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
                                              volatile int* abort_flag, int* status) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+  for (int spin = 0; spin < 64; ++spin)
+    if (ptx::mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int spin = 0; spin < 64; ++spin)
+      if (ptx::mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kTimeoutCycles) {
       *abort_flag = 1;
@@ -328,11 +347,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tp[i].n > 0) ok = bounded_wait(&bars.q_full[i], 0, abort_flag, p.status);
       for (int t = -1; t < nmax && ok; ++t) {
         // S_i(t+1) = Q_i K(t+1)^T
+        FA8_TR(2, t + 1, 0);
         if (t + 1 < nmax) {
           const int L = 2 * (t + 1);
           const int st = L % NS;
           ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
           if (!ok) break;
+          FA8_TR(2, t + 1, 1);
           const uint32_t k_addr = s_base + C::kOffRing + st * C::kStageBytes;
           for (int i = 0; i < kTilesPerCta; ++i) {
             const int tl = t + 1 - start[i];
@@ -350,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            kk > 0 ? 1u : 0u);
             }
             ptx::umma_commit(&bars.s_full[i]);
+            FA8_TR(2, t + 1, 2 + i);
           }
           if (!ok) break;
           ptx::umma_commit(&bars.kv_empty[st]);
@@ -360,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int st = L % NS;
           ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
           if (!ok) break;
+          FA8_TR(2, t + 1, 4);
           const uint32_t v_addr = s_base + C::kOffRing + st * C::kStageBytes;
           for (int i = 0; i < kTilesPerCta; ++i) {
             const int tl = t - start[i];
@@ -382,6 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             ptx::umma_commit(&bars.o_done[i]);
+            FA8_TR(2, t + 1, 5 + i);
           }
           if (!ok) break;
           ptx::umma_commit(&bars.kv_empty[st]);
@@ -412,7 +436,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     for (int tl = 0; tl < n && ok; ++tl) {
       const int kv = n - 1 - tl;
+      if (r == 0) FA8_TR(i, tl, 0);
       ok = bounded_wait(&bars.s_full[i], tl & 1, abort_flag, p.status);
+      if (r == 0) FA8_TR(i, tl, 1);
       if (!ok) break;
       ptx::tc_fence_after();
       float s[kBlockN];
@@ -431,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars.s_free[i]);
+      if (r == 0) FA8_TR(i, tl, 2);
 
       // Mask: keys past seqlen_kv, and (causal) keys after this query.
       const int kv0 = kv * kBlockN;
@@ -442,9 +469,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kBlockN; ++c)
           if (c >= li) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      // Row max: eight independent three-input max chains, then a short tree.
+      float mx8[8];
 #pragma unroll
-      for (int c = 1; c < kBlockN; ++c) mx = fmaxf(mx, s[c]);
+      for (int g = 0; g < 8; ++g) {
+        float a = ptx::fmax3(s[16 * g + 0], s[16 * g + 1], s[16 * g + 2]);
+#pragma unroll
+        for (int c = 3; c < 15; c += 2) a = ptx::fmax3(a, s[16 * g + c], s[16 * g + c + 1]);
+        mx8[g] = fmaxf(a, s[16 * g + 15]);
+      }
+      const float mx = ptx::fmax3(ptx::fmax3(mx8[0], mx8[1], mx8[2]),
+                                  ptx::fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
       const float m_tile = mx * sl2;
       const float m_new = fmaxf(m_run, m_tile);
       const bool need = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold || tl == 0);
@@ -454,19 +489,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (need) alpha = (m_run == -INFINITY) ? 0.f : ptx::ex2(m_run - m_use);
       m_run = m_use;
 
-      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+      // p = 2^(s * scale * log2e - base): packed FMA, MUFU ex2, packed sums.
+      const uint64_t sl2x2 = ptx::pack2(sl2, sl2);
+      const uint64_t nbx2 = ptx::pack2(-base, -base);
+      uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-      for (int c = 0; c < kBlockN; c += 4) {
-        s[c + 0] = ptx::ex2(fmaf(s[c + 0], sl2, -base));
-        s[c + 1] = ptx::ex2(fmaf(s[c + 1], sl2, -base));
-        s[c + 2] = ptx::ex2(fmaf(s[c + 2], sl2, -base));
-        s[c + 3] = ptx::ex2(fmaf(s[c + 3], sl2, -base));
-        sum0 += s[c + 0];
-        sum1 += s[c + 1];
-        sum2 += s[c + 2];
-        sum3 += s[c + 3];
+      for (int c = 0; c < kBlockN; c += 2) {
+        const uint64_t x = ptx::ffma2(ptx::pack2(s[c], s[c + 1]), sl2x2, nbx2);
+        float x0, x1;
+        ptx::unpack2(x, x0, x1);
+        s[c] = ptx::ex2(x0);
+        s[c + 1] = ptx::ex2(x1);
+        acc[(c / 2) % 4] = ptx::fadd2(acc[(c / 2) % 4], ptx::pack2(s[c], s[c + 1]));
       }
-      l_run = l_run * alpha + ((sum0 + sum1) + (sum2 + sum3));
+      {
+        const uint64_t a01 = ptx::fadd2(acc[0], acc[1]);
+        const uint64_t a23 = ptx::fadd2(acc[2], acc[3]);
+        float u0, u1;
+        ptx::unpack2(ptx::fadd2(a01, a23), u0, u1);
+        l_run = l_run * alpha + (u0 + u1);
+      }
 
       // e4m3 P (hi) and, for split tiles, the e4m3 residual P - hi (lo).
       uint32_t ph[kBlockN / 4];
@@ -474,24 +516,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool split = tp[i].split != 0;
 #pragma unroll
       for (int j = 0; j < kBlockN / 4; ++j) {
-        ph[j] = (uint32_t)ptx::cvt_e4m3x2(s[4 * j], s[4 * j + 1]) |
-                ((uint32_t)ptx::cvt_e4m3x2(s[4 * j + 2], s[4 * j + 3]) << 16);
+        ph[j] = ptx::cvt_e4m3x4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
         if (split) {
           const uint32_t h01 = ptx::cvt_e4m3x2_to_f16x2((uint16_t)(ph[j] & 0xffffu));
           const uint32_t h23 = ptx::cvt_e4m3x2_to_f16x2((uint16_t)(ph[j] >> 16));
           const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
           const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-          pl[j] = (uint32_t)ptx::cvt_e4m3x2(s[4 * j] - f01.x, s[4 * j + 1] - f01.y) |
-                  ((uint32_t)ptx::cvt_e4m3x2(s[4 * j + 2] - f23.x, s[4 * j + 3] - f23.y) << 16);
+          pl[j] = ptx::cvt_e4m3x4(s[4 * j] - f01.x, s[4 * j + 1] - f01.y, s[4 * j + 2] - f23.x,
+                                  s[4 * j + 3] - f23.y);
         } else {
           pl[j] = 0u;
         }
       }
 
       // PV(t-1) must be complete before O is rescaled or P overwritten.
+      if (r == 0) FA8_TR(i, tl, 3);
       if (tl > 0) {
         ok = bounded_wait(&bars.o_done[i], (tl - 1) & 1, abort_flag, p.status);
         if (!ok) break;
+        if (r == 0) FA8_TR(i, tl, 4);
         ptx::tc_fence_after();
         if (need) {
 #pragma unroll
@@ -523,6 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars.p_full[i]);
+      if (r == 0) FA8_TR(i, tl, 5);
     }
 
     // Epilogue: O / l -> global, LSE.

@@ -1,0 +1,405 @@
+#!/usr/bin/env python
+"""Benchmark of the sm_100a FP8 attention forward (one JSON line on rank 0).
+
+Workload (the headline): B=4, H=32, S=4096, D=128,
+non-causal, Q/K/V ~ N(0,1) cast to e4m3, V pre-transposed (B,H,D,S), fp16 O.
+One "step" = one forward over that batch. With N GPUs each rank runs its own
+copy of the headline batch (B=4 per GPU, global batch 4N, weak scaling):
+the (batch, head) units are sharded across ranks with no collective on the
+data path; the only communication is the timing barrier and the max-reduce
+of the elapsed time.
+
+Arms:
+  (default)          this framework: device-resident inputs (`value`) and the
+                     end-to-end path through the public API with pinned host
+                     buffers and host<->device copies in the timed region (`e2e`).
+  --impl reference   the reference's CPU path (test.py:8-15 naive attention,
+                     restated in fp32 by oracle/attention_ref.py) on this host's
+                     cores, over a bounded sample of the same workload.
+
+Inputs (Q/K/V 192 MiB + O 128 MiB per GPU) exceed the 126 MB L2, so no L2
+flush is needed between timed steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOAD = dict(name="C2", batch=4, heads=32, seqlen=4096, head_dim=128, causal=False,
+                dist="normal", sigma=1.0, seed=1234)
+METRIC = "FP8 attn fwd TFLOPS/GPU and % of FP8 dense peak; ms/call at 1/2/4/8 B200"
+FP8_SPEC_TFLOPS = 4500.0
+
+
+def flops(batch, heads, sq, skv, d, causal):
+    f = 4.0 * batch * heads * sq * skv * d
+    return f / 2 if causal else f
+
+
+def algo_bytes(batch, heads, sq, skv, d):
+    return batch * heads * (sq * d + 2 * skv * d) + batch * heads * sq * d * 2
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per launch from the committed ncu summary (None if absent)."""
+    p = ROOT / "profiles" / "fa8_fwd_kernel_c2.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        # under load = power well above idle
+        pmax = max(r[2] for r in rows)
+        loaded = [r for r in rows if r[2] > 0.5 * pmax] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3])
+                          if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded),
+                "sm_max_mhz": max(r[1] for r in loaded),
+                "power_w_max": pmax, "samples": len(loaded), "reasons": reasons}
+
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def make_inputs_dev(device, rank):
+    """This rank's shard: B=4 (per GPU) x H x S x D, seeded per global (batch) index."""
+    import torch
+
+    W = WORKLOAD
+    B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
+    seed = W["seed"] + 1000 * rank
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    # Drawn on the host (the e2e arm copies them from pinned memory), cast to
+    # e4m3 with scale 1.0 (round to nearest even).
+    q = (torch.randn((B, H, S, D), generator=gen) * W["sigma"]).to(torch.float8_e4m3fn)
+    k = (torch.randn((B, H, S, D), generator=gen) * W["sigma"]).to(torch.float8_e4m3fn)
+    v = (torch.randn((B, H, D, S), generator=gen) * W["sigma"]).to(torch.float8_e4m3fn)
+    return q, k, v
+
+
+def fp8_gemm_probe(device):
+    """Dense e4m3 GEMM throughput on this GPU via torch._scaled_mm (cuBLASLt), TFLOP/s."""
+    import torch
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=device).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=device)
+        for _ in range(3):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = 1e9
+        for _ in range(5):
+            e0.record()
+            for _ in range(10):
+                torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1) / 10)
+        del a, b
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    except Exception:  # noqa: BLE001 - probe is informational
+        return None
+
+
+def cpu_baseline_sample(max_seconds=12.0):
+    """test.py's naive attention (fp32, CPU oracle) on a bounded sample of the workload.
+
+    Times whole (batch, head) units of the headline shape; returns TFLOPS and a
+    description. Runs with every host thread numpy's BLAS is allowed to use.
+    """
+    import numpy as np
+    from oracle.attention_ref import attention, e4m3_decode, make_inputs
+
+    W = WORKLOAD
+    S, D = W["seqlen"], W["head_dim"]
+    q = e4m3_decode(make_inputs((1, 1, S, D), W["dist"], 1, W["sigma"]))
+    k = e4m3_decode(make_inputs((1, 1, S, D), W["dist"], 2, W["sigma"]))
+    v = e4m3_decode(make_inputs((1, 1, D, S), W["dist"], 3, W["sigma"]))
+    attention(q, k, v, W["causal"])  # warm-up
+    units, t0 = 0, time.perf_counter()
+    while True:
+        attention(q, k, v, W["causal"])
+        units += 1
+        el = time.perf_counter() - t0
+        if el > max_seconds or units >= 64:
+            break
+    f = flops(1, units, S, S, D, W["causal"])
+    return f / el / 1e12, units, el
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    W = WORKLOAD
+    cores = os.cpu_count()
+    vals = []
+    per_step = max(2.0, 60.0 / max(1, args.steps + args.warmup))
+    for i in range(args.warmup + args.steps):
+        tf, units, el = cpu_baseline_sample(max_seconds=per_step)
+        if i >= args.warmup:
+            vals.append(tf)
+    v = statistics.median(vals)
+    total_flops = flops(W["batch"], W["heads"], W["seqlen"], W["seqlen"], W["head_dim"],
+                        W["causal"])
+    sample = (f"{units} of {W['batch'] * W['heads']} (batch, head) units of the workload per "
+              f"step, extrapolated by FLOPs")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_flops / (v * 1e12) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C2 B4 H32 S4096 D128 non-causal (BASELINE configs[1])",
+                   "global_batch": W["batch"], "seq_len": W["seqlen"], "heads": W["heads"],
+                   "head_dim": W["head_dim"], "causal": False,
+                   "path": "test.py:8-15 naive attention, fp32 numpy on host cores "
+                           "(oracle/attention_ref.py)"},
+        "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_framework(args):
+    import torch
+
+    world, rank, local = dist_setup(args)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    import ada_cute_fp8_flash_attention_b200 as fa8
+
+    W = WORKLOAD
+    B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
+    causal = W["causal"]
+    q_h, k_h, v_h = make_inputs_dev(device, rank)
+    q, k, v = q_h.to(device), k_h.to(device), v_h.to(device)
+    out = torch.empty((B, H, S, D), dtype=torch.float16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    step = lambda: fa8.flash_attn_fp8_forward_ex(q, k, v, causal=causal, out=out)  # noqa: E731
+
+    # ---- device-resident timed region
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = fa8.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    launches = fa8.launch_count() - launches0
+    ms_local = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(ms_local)
+    ms_step = ms / args.steps
+    f_rank = flops(B, H, S, S, D, causal)
+    total_flops = f_rank * world
+    value = total_flops / (ms_step * 1e-3) / 1e12  # whole-job TFLOPS
+    kern_tflops = f_rank / (ms_local / args.steps * 1e-3) / 1e12  # this rank's kernel
+
+    # ---- end-to-end through the public API with pinned host buffers
+    qp, kp, vp = q_h.pin_memory(), k_h.pin_memory(), v_h.pin_memory()
+    op = torch.empty((B, H, S, D), dtype=torch.float16).pin_memory()
+    e_steps = 0 if args.no_e2e else max(2, min(args.steps, 10))
+
+    def e2e_step():
+        qd = qp.to(device, non_blocking=True)
+        kd = kp.to(device, non_blocking=True)
+        vd = vp.to(device, non_blocking=True)
+        o = fa8.flash_attn_fp8_forward_ex(qd, kd, vd, causal=causal)
+        op.copy_(o, non_blocking=True)
+
+    e_ms, e2e_val = None, None
+    if e_steps:
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = max_over_ranks(e0.elapsed_time(e1)) / e_steps
+        e2e_val = total_flops / (e_ms * 1e-3) / 1e12
+    h2d = q.numel() + k.numel() + v.numel()
+    d2h = op.numel() * 2
+
+    probe = fp8_gemm_probe(device) if rank == 0 else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tf, units, el = cpu_baseline_sample(max_seconds=args.cpu_seconds)
+        cpu = {"value": tf, "unit": "TFLOPS", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{units} (batch, head) units of the workload (S=4096, D=128, "
+                         f"non-causal) in {el:.1f}s, test.py:8-15 math in fp32 numpy"}
+
+    if rank == 0:
+        hbm, bf16, src = load_peaks()
+        fp8_peak = 2.0 * bf16
+        traffic = load_traffic()
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3", "data": "synthetic",
+            "config": {"workload": "C2 B4 H32 S4096 D128 non-causal (BASELINE configs[1]), "
+                                   "per GPU", "global_batch": B * world, "seq_len": S,
+                       "heads": H, "head_dim": D, "causal": causal,
+                       "parallelism": f"dp{world} over (batch, head), no collective",
+                       "l2": "inputs larger than L2 (Q/K/V 192 MiB + O 128 MiB per GPU)"},
+            "tflops_per_gpu": value / world,
+            "pct_fp8_spec_peak": 100.0 * value / world / FP8_SPEC_TFLOPS,
+            "pct_fp8_2x_measured_bf16": 100.0 * value / world / fp8_peak,
+            "fp8_gemm_probe_tflops": probe,
+            "roofline": {"bound": "tensor", "achieved": kern_tflops, "peak": fp8_peak,
+                         "unit": "TFLOP/s", "frac": kern_tflops / fp8_peak,
+                         "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); "
+                                        "FP8 tensor rate is twice bf16",
+                         "frac_of_spec_4500": kern_tflops / FP8_SPEC_TFLOPS,
+                         "frac_of_fp8_gemm_probe": (kern_tflops / probe) if probe else None,
+                         "algorithmic_flops_per_launch": f_rank,
+                         "hbm_gbs": algo_bytes(B, H, S, S, D) / (ms_local / args.steps * 1e-3) / 1e9,
+                         "traffic": traffic},
+            "e2e": {"value": e2e_val, "unit": "TFLOPS", "ms_per_step": e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "flash_attn_fp8_forward_ex with pinned host Q/K/V and O"},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="framework", choices=["framework", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e arm")
+    ap.add_argument("--shape", default=None,
+                    help="B,H,S,D,causal override for profiling runs (not a bench line)")
+    args = ap.parse_args()
+    if args.shape:
+        b, h, s, d, c = args.shape.split(",")
+        WORKLOAD.update(batch=int(b), heads=int(h), seqlen=int(s), head_dim=int(d),
+                        causal=c.lower() in ("1", "true", "causal", "c"))
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_framework(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
