@@ -12,8 +12,8 @@ Lemon7-UP/ada_cute_fp8_flash_attention, whose only export is
 The computation runs in the native library ``libfa8.so`` (C ABI,
 ``include/fa8.h``) through the PyTorch extension ``_fa8_torch``. There is no
 CPU or eager-PyTorch fallback: importing this package raises ImportError when
-the native extension has not been built (``python -m
-ada_cute_fp8_flash_attention_b200._build``).
+the native extension has not been built (``python
+ada_cute_fp8_flash_attention_b200/_build.py``).
 """
 from __future__ import annotations
 
@@ -36,7 +36,7 @@ def _load_ext():
     if not path.exists():
         raise ImportError(
             f"native extension {path.name} is not built; run "
-            "`python -m ada_cute_fp8_flash_attention_b200._build` (no CPU fallback exists)")
+            "`python ada_cute_fp8_flash_attention_b200/_build.py` (no CPU fallback exists)")
     import torch  # noqa: F401  (loads libc10 / libtorch for the extension)
 
     name = f"{__name__}.{_build.EXT_NAME}"

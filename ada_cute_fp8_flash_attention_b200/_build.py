@@ -33,7 +33,7 @@ NVCC_FLAGS = [
 ]
 
 CUDA_SOURCES = ["fa8_api.cu", "fa8_aux.cu"]
-CUDA_HEADERS = ["fa8_fwd_kernel.cuh", "sm100_ptx.cuh"]
+CUDA_HEADERS = ["fa8_fwd_kernel.cuh", "fa8_softmax.cuh", "sm100_ptx.cuh"]
 
 
 def _nvcc() -> str:

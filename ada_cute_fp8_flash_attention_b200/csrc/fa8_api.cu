@@ -247,6 +247,12 @@ uint64_t fa8_launch_count(void) { return g_launches.load(std::memory_order_relax
 }  // extern "C"
 
 #ifdef FA8_TRACE
+extern "C" int fa8_trace_cta_fetch(long long* host_buf) {
+  return cudaMemcpyFromSymbol(host_buf, fa8::fa8_trace_cta, sizeof(fa8::fa8_trace_cta)) ==
+                 cudaSuccess
+             ? 0
+             : 1;
+}
 extern "C" int fa8_trace_fetch(long long* host_buf) {
   return cudaMemcpyFromSymbol(host_buf, fa8::fa8_trace_buf, sizeof(fa8::fa8_trace_buf)) ==
                  cudaSuccess

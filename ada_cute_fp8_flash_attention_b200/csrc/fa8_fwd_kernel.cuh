@@ -6,11 +6,12 @@
 // with a Blackwell design:
 //
 //   * one CTA owns two 128-row query tiles (Q0, Q1) of one (batch, head);
-//   * 384 threads = three warpgroups; warps 10-11 of the control warpgroup
-//     are idle;
+//   * 384 threads = three warpgroups; warp 11 of the control warpgroup is
+//     idle;
 //   * warp 9 (TMA) streams K and V tiles (128 keys each) into a ring of
 //     shared-memory stages (cp.async.bulk.tensor, mbarrier completion);
-//   * warp 8 (one elected thread) issues tcgen05.mma kind::f8f6f4:
+//   * warps 8 and 10 (one elected thread each, one per query tile) issue
+//     tcgen05.mma kind::f8f6f4:
 //       S_i = Q_i K^T  into TMEM (128 lanes x 128 f32 columns per tile),
 //       O_i += P_i V   into TMEM (128 lanes x D f32 columns per tile);
 //   * warps 0-3 and 4-7 are the softmax warpgroups of Q0 and Q1. Each thread
@@ -51,6 +52,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "fa8_softmax.cuh"
 #include "sm100_ptx.cuh"
 
 namespace fa8 {
@@ -61,8 +63,18 @@ constexpr int kBlockN = 128;           // keys per K/V tile
 constexpr int kTilesPerCta = 2;        // query tiles per CTA
 constexpr int kMmaWarp = 8;
 constexpr int kLoadWarp = 9;
-constexpr float kPShift = 6.0f;        // log2 of the P scale-up
-constexpr float kRescaleThreshold = 2.0f;  // log2 units
+constexpr int kMmaWarp2 = 10;
+#ifndef FA8_EMU
+#define FA8_EMU 0
+#endif
+// Columns of every 8 whose exp2 runs on the FMA pipe instead of MUFU. Measured
+// on B200: 0 is fastest in this kernel (the emulation adds issue pressure and
+// spills at the 168-register budget).
+constexpr int kEmuPer8 = FA8_EMU;
+#ifndef FA8_STAGGER
+#define FA8_STAGGER 1
+#endif
+constexpr bool kStagger = FA8_STAGGER != 0;
 constexpr long long kTimeoutCycles = 4000000000LL;
 constexpr int kDefaultSplitKeys = 1024;
 
@@ -105,6 +117,13 @@ struct KernelParams {
 // Debug-only phase timestamps (clock64) of CTA (0,0,0): [role][step][event].
 // role 0/1 = softmax warpgroup 0/1 (thread 0 of the group), role 2 = MMA thread.
 __device__ long long fa8_trace_buf[3][64][8];
+// Per-CTA (linear block id < 4096): globaltimer at entry and exit, SM id.
+__device__ long long fa8_trace_cta[4096][3];
+__device__ __forceinline__ long long fa8_gtimer() {
+  long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 #define FA8_TR(role, step, ev)                                                 \
   do {                                                                         \
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (step) < 64)  \
@@ -126,7 +145,8 @@ struct Bars {
   uint64_t s_free[kTilesPerCta];
   uint64_t p_full[kTilesPerCta];
   uint64_t o_done[kTilesPerCta];
-  uint64_t drain;
+  uint64_t drain[kTilesPerCta];
+  uint64_t offset;  // softmax warpgroup 0 -> 1: first exp phase finished
 };
 
 // Bounded wait on phase `parity` of `bar`. Returns false on abort/timeout.
@@ -222,6 +242,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+#ifdef FA8_TRACE
+  const int cta_lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (threadIdx.x == 0 && cta_lin < 4096) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %smid;" : "=r"(smid));
+    fa8_trace_cta[cta_lin][0] = fa8_gtimer();
+    fa8_trace_cta[cta_lin][2] = smid;
+  }
+#endif
   const int qb = p.causal ? (p.n_qblocks - 1 - (int)blockIdx.x) : (int)blockIdx.x;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
@@ -268,9 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < NS; ++s) {
       ptx::mbar_init(&bars.kv_full[s], 1);
-      ptx::mbar_init(&bars.kv_empty[s], 1);
+      ptx::mbar_init(&bars.kv_empty[s], kTilesPerCta);
     }
-    ptx::mbar_init(&bars.drain, 1);
+    for (int i = 0; i < kTilesPerCta; ++i) ptx::mbar_init(&bars.drain[i], 1);
+    ptx::mbar_init(&bars.offset, 4);
     abort_sh = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
@@ -334,47 +364,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == kMmaWarp || warp == kMmaWarp2) {
+    // ------------------------------------------------------------ MMA issuers
+    // One issuing thread per query tile (warp 8: Q0, warp 10: Q1), so each
+    // tile's QK -> softmax -> PV chain advances at its own pace; the two
+    // softmax warpgroups are not forced into lockstep by a shared in-order
+    // issue queue. Both threads release every K/V stage (kv_empty counts 2).
     if (lane == 0) {
-      const uint32_t q_addr[2] = {s_base + C::kOffQ, s_base + C::kOffQ + C::kQBytes};
-      const uint32_t p_hi[2] = {s_base + C::kOffP, s_base + C::kOffP + C::kPBytes};
-      const uint32_t p_lo[2] = {s_base + C::kOffP + 2 * C::kPBytes,
-                                s_base + C::kOffP + 3 * C::kPBytes};
-      const int start[2] = {nmax - tp[0].n, nmax - tp[1].n};
+      const int i = (warp == kMmaWarp) ? 0 : 1;
+      const uint32_t q_addr = s_base + C::kOffQ + i * C::kQBytes;
+      const uint32_t p_hi = s_base + C::kOffP + i * C::kPBytes;
+      const uint32_t p_lo = s_base + C::kOffP + (2 + i) * C::kPBytes;
+      const int start = nmax - tp[i].n;
+      const bool active = tp[i].n > 0;
+      const int role = 2 + i;
       bool ok = true;
-      for (int i = 0; i < kTilesPerCta && ok; ++i)
-        if (tp[i].n > 0) ok = bounded_wait(&bars.q_full[i], 0, abort_flag, p.status);
+      if (active) ok = bounded_wait(&bars.q_full[i], 0, abort_flag, p.status);
       for (int t = -1; t < nmax && ok; ++t) {
         // S_i(t+1) = Q_i K(t+1)^T
-        FA8_TR(2, t + 1, 0);
+        if (i == 0) FA8_TR(2, t + 1, 0);
         if (t + 1 < nmax) {
           const int L = 2 * (t + 1);
           const int st = L % NS;
           ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
           if (!ok) break;
-          FA8_TR(2, t + 1, 1);
-          const uint32_t k_addr = s_base + C::kOffRing + st * C::kStageBytes;
-          for (int i = 0; i < kTilesPerCta; ++i) {
-            const int tl = t + 1 - start[i];
-            if (tp[i].n == 0 || tl < 0) continue;
+          if (i == 0) FA8_TR(2, t + 1, 1);
+          const int tl = t + 1 - start;
+          if (active && tl >= 0) {
             if (tl > 0) {
               ok = bounded_wait(&bars.s_free[i], (tl - 1) & 1, abort_flag, p.status);
               if (!ok) break;
             }
             ptx::tc_fence_after();
+            const uint32_t k_addr = s_base + C::kOffRing + st * C::kStageBytes;
             const uint32_t d_tmem = tmem + C::kColS + i * kBlockN;
 #pragma unroll
             for (int kk = 0; kk < D / 32; ++kk) {
-              ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(q_addr[i] + kk * 32, C::kQKRowBytes),
+              ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(q_addr + kk * 32, C::kQKRowBytes),
                            ptx::smem_desc_kmajor(k_addr + kk * 32, C::kQKRowBytes), C::kIdescS,
                            kk > 0 ? 1u : 0u);
             }
             ptx::umma_commit(&bars.s_full[i]);
-            FA8_TR(2, t + 1, 2 + i);
+            if (i == 0) FA8_TR(2, t + 1, 2);
+            ptx::umma_commit(&bars.kv_empty[st]);
+          } else {
+            ptx::mbar_arrive(&bars.kv_empty[st]);
           }
-          if (!ok) break;
-          ptx::umma_commit(&bars.kv_empty[st]);
         }
         // O_i += P_i(t) V(t)
         if (t >= 0) {
@@ -382,39 +417,40 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int st = L % NS;
           ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
           if (!ok) break;
-          FA8_TR(2, t + 1, 4);
-          const uint32_t v_addr = s_base + C::kOffRing + st * C::kStageBytes;
-          for (int i = 0; i < kTilesPerCta; ++i) {
-            const int tl = t - start[i];
-            if (tp[i].n == 0 || tl < 0) continue;
+          if (i == 0) FA8_TR(2, t + 1, 4);
+          const int tl = t - start;
+          if (active && tl >= 0) {
             ok = bounded_wait(&bars.p_full[i], tl & 1, abort_flag, p.status);
             if (!ok) break;
             ptx::tc_fence_after();
+            const uint32_t v_addr = s_base + C::kOffRing + st * C::kStageBytes;
             const uint32_t d_tmem = tmem + C::kColO + i * D;
 #pragma unroll
             for (int kk = 0; kk < kBlockN / 32; ++kk) {
-              ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_hi[i] + kk * 32, 128),
+              ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_hi + kk * 32, 128),
                            ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO,
                            (tl > 0 || kk > 0) ? 1u : 0u);
             }
             if (tp[i].split) {
 #pragma unroll
               for (int kk = 0; kk < kBlockN / 32; ++kk) {
-                ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_lo[i] + kk * 32, 128),
+                ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_lo + kk * 32, 128),
                              ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO, 1u);
               }
             }
             ptx::umma_commit(&bars.o_done[i]);
-            FA8_TR(2, t + 1, 5 + i);
+            if (i == 0) FA8_TR(2, t + 1, 5);
+            ptx::umma_commit(&bars.kv_empty[st]);
+          } else {
+            ptx::mbar_arrive(&bars.kv_empty[st]);
           }
-          if (!ok) break;
-          ptx::umma_commit(&bars.kv_empty[st]);
         }
       }
-      // Drain every MMA issued before TMEM is freed.
-      ptx::umma_commit(&bars.drain);
+      (void)role;
+      // Drain every MMA this thread issued before TMEM is freed.
+      ptx::umma_commit(&bars.drain[i]);
       const long long t0 = clock64();
-      while (!ptx::mbar_try_wait(&bars.drain, 0) && clock64() - t0 < kTimeoutCycles) {
+      while (!ptx::mbar_try_wait(&bars.drain[i], 0) && clock64() - t0 < kTimeoutCycles) {
       }
     }
   } else if (warp < 8) {
@@ -433,6 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_run = -INFINITY;  // running max of s*scale*log2e
     float l_run = 0.f;
     bool ok = true;
+    bool offset_sent = false;
 
     for (int tl = 0; tl < n && ok; ++tl) {
       const int kv = n - 1 - tl;
@@ -469,65 +506,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kBlockN; ++c)
           if (c >= li) s[c] = -INFINITY;
       }
-      // Row max: eight independent three-input max chains, then a short tree.
-      float mx8[8];
-#pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        float a = ptx::fmax3(s[16 * g + 0], s[16 * g + 1], s[16 * g + 2]);
-#pragma unroll
-        for (int c = 3; c < 15; c += 2) a = ptx::fmax3(a, s[16 * g + c], s[16 * g + c + 1]);
-        mx8[g] = fmaxf(a, s[16 * g + 15]);
-      }
-      const float mx = ptx::fmax3(ptx::fmax3(mx8[0], mx8[1], mx8[2]),
-                                  ptx::fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-      const float m_tile = mx * sl2;
-      const float m_new = fmaxf(m_run, m_tile);
-      const bool need = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold || tl == 0);
-      const float m_use = need ? m_new : m_run;
-      const float base = (m_use == -INFINITY) ? 0.f : (m_use - kPShift);
-      float alpha = 1.f;
-      if (need) alpha = (m_run == -INFINITY) ? 0.f : ptx::ex2(m_run - m_use);
-      m_run = m_use;
-
-      // p = 2^(s * scale * log2e - base): packed FMA, MUFU ex2, packed sums.
-      const uint64_t sl2x2 = ptx::pack2(sl2, sl2);
-      const uint64_t nbx2 = ptx::pack2(-base, -base);
-      uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-      for (int c = 0; c < kBlockN; c += 2) {
-        const uint64_t x = ptx::ffma2(ptx::pack2(s[c], s[c + 1]), sl2x2, nbx2);
-        float x0, x1;
-        ptx::unpack2(x, x0, x1);
-        s[c] = ptx::ex2(x0);
-        s[c + 1] = ptx::ex2(x1);
-        acc[(c / 2) % 4] = ptx::fadd2(acc[(c / 2) % 4], ptx::pack2(s[c], s[c + 1]));
-      }
-      {
-        const uint64_t a01 = ptx::fadd2(acc[0], acc[1]);
-        const uint64_t a23 = ptx::fadd2(acc[2], acc[3]);
-        float u0, u1;
-        ptx::unpack2(ptx::fadd2(a01, a23), u0, u1);
-        l_run = l_run * alpha + (u0 + u1);
-      }
-
-      // e4m3 P (hi) and, for split tiles, the e4m3 residual P - hi (lo).
       uint32_t ph[kBlockN / 4];
       uint32_t pl[kBlockN / 4];
       const bool split = tp[i].split != 0;
-#pragma unroll
-      for (int j = 0; j < kBlockN / 4; ++j) {
-        ph[j] = ptx::cvt_e4m3x4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
-        if (split) {
-          const uint32_t h01 = ptx::cvt_e4m3x2_to_f16x2((uint16_t)(ph[j] & 0xffffu));
-          const uint32_t h23 = ptx::cvt_e4m3x2_to_f16x2((uint16_t)(ph[j] >> 16));
-          const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
-          const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-          pl[j] = ptx::cvt_e4m3x4(s[4 * j] - f01.x, s[4 * j + 1] - f01.y, s[4 * j + 2] - f23.x,
-                                  s[4 * j + 3] - f23.y);
-        } else {
-          pl[j] = 0u;
-        }
+      if (kStagger && i == 1 && tl == 0) {
+        // Start one exp phase behind warpgroup 0 so that one group's barrier
+        // waits, S loads and P stores overlap the other's exp work.
+        ok = bounded_wait(&bars.offset, 0, abort_flag, p.status);
+        if (!ok) break;
       }
+      const StepOut so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, split, m_run,
+                                                             l_run, ph, pl);
+      if (kStagger && i == 0 && tl == 0) {
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars.offset);
+        offset_sent = true;
+      }
+      const bool need = so.need;
+      const float alpha = so.alpha;
 
       // PV(t-1) must be complete before O is rescaled or P overwritten.
       if (r == 0) FA8_TR(i, tl, 3);
@@ -569,6 +565,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (r == 0) FA8_TR(i, tl, 5);
     }
 
+    if (kStagger && i == 0 && !offset_sent) {
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars.offset);
+    }
     // Epilogue: O / l -> global, LSE.
     if (n > 0 && ok) ok = bounded_wait(&bars.o_done[i], (n - 1) & 1, abort_flag, p.status);
     if (tp[i].q_start < p.seqlen_q) {
@@ -606,6 +606,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, C::kTmemCols);
   }
+#ifdef FA8_TRACE
+  if (threadIdx.x == 0 && cta_lin < 4096) fa8_trace_cta[cta_lin][1] = fa8_gtimer();
+#endif
 }
 
 }  // namespace fa8

@@ -1,0 +1,151 @@
+// fa8_softmax.cuh — per-row online-softmax step of the FP8 attention kernel.
+//
+// One thread owns one query row and holds that row's NC scores of the
+// current K/V tile in registers (loaded from TMEM). The step:
+//   1. row max (three-input max chains),
+//   2. warp-uniform lazy-rescale decision: the reference rescales O on every
+//      tile (csrc/flash_attention.cu:80-86); here the running max only moves
+//      (and O is rescaled) when some row of the warp grew by more than
+//      kRescaleThreshold in log2 units,
+//   3. p = 2^(s * scale * log2e - (m - kPShift)) for every column. MUFU ex2
+//      by default; kEmuPer8 of every 8 columns can instead use a polynomial
+//      exp2 on the FMA pipe (range reduction x = n + f with n = round(x) via
+//      the 1.5 * 2^23 magic constant, degree-3 polynomial for 2^f on
+//      [-0.5, 0.5] fitted by iterated weighted least squares to a relative
+//      error of 7.7e-5, then n added to the exponent field with an integer
+//      multiply-add),
+//   4. row sum of fp32 p (packed f32x2 adds),
+//   5. e4m3 requantisation of P (hi) and, for split tiles, of P - hi (lo).
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+
+namespace fa8 {
+
+constexpr float kPShift = 6.0f;            // log2 of the P scale-up
+constexpr float kRescaleThreshold = 2.0f;  // log2 units; kPShift + it <= log2(448)
+
+namespace emu {
+// 2^f on [-0.5, 0.5]: c0 + f (c1 + f (c2 + f c3)), max relative error 7.7e-5.
+constexpr float kC0 = 0.999928891658783f;
+constexpr float kC1 = 0.6932758092880249f;
+constexpr float kC2 = 0.24260424077510834f;
+constexpr float kC3 = 0.05509091913700104f;
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + magic rounds x to an integer
+constexpr float kClampLo = -30.0f;     // 2^-30 is far below e4m3's smallest subnormal
+}  // namespace emu
+
+// Polynomial exp2 of a packed pair (FMA pipe + two integer multiply-adds).
+__device__ __forceinline__ uint64_t exp2_emu_pair(float x0, float x1) {
+  x0 = fmaxf(x0, emu::kClampLo);
+  x1 = fmaxf(x1, emu::kClampLo);
+  const uint64_t x = ptx::pack2(x0, x1);
+  const uint64_t t = ptx::fadd2(x, ptx::pack2(emu::kMagic, emu::kMagic));
+  const uint64_t n = ptx::fadd2(t, ptx::pack2(-emu::kMagic, -emu::kMagic));
+  const uint64_t f = ptx::ffma2(n, ptx::pack2(-1.f, -1.f), x);
+  uint64_t p = ptx::ffma2(ptx::pack2(emu::kC3, emu::kC3), f, ptx::pack2(emu::kC2, emu::kC2));
+  p = ptx::ffma2(p, f, ptx::pack2(emu::kC1, emu::kC1));
+  p = ptx::ffma2(p, f, ptx::pack2(emu::kC0, emu::kC0));
+  // bits(t) = bits(magic) + n; (bits(t) << 23) == n << 23 modulo 2^32.
+  uint32_t t0, t1, p0, p1;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t));
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(p0), "=r"(p1) : "l"(p));
+  uint32_t r0, r1;
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(r0) : "r"(t0), "r"(p0));
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(r1) : "r"(t1), "r"(p1));
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(r0), "r"(r1));
+  return r;
+}
+
+// Result of one softmax step for the owning thread's row.
+struct StepOut {
+  float alpha;  // factor to apply to the row's O accumulator (1 if !need)
+  bool need;    // warp-uniform: O must be rescaled by alpha
+};
+
+template <int NC, int kEmuPer8>
+__device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, bool first,
+                                                    bool split, float& m_run, float& l_run,
+                                                    uint32_t (&ph)[NC / 4],
+                                                    uint32_t (&pl)[NC / 4]) {
+  static_assert(NC % 16 == 0, "row length must be a multiple of 16");
+  // 1. row max
+  constexpr int G = NC / 16;
+  float mxg[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float a = ptx::fmax3(s[16 * g + 0], s[16 * g + 1], s[16 * g + 2]);
+#pragma unroll
+    for (int c = 3; c < 15; c += 2) a = ptx::fmax3(a, s[16 * g + c], s[16 * g + c + 1]);
+    mxg[g] = fmaxf(a, s[16 * g + 15]);
+  }
+  float mx = mxg[0];
+#pragma unroll
+  for (int g = 1; g < G; ++g) mx = fmaxf(mx, mxg[g]);
+
+  // 2. lazy rescale decision
+  StepOut out;
+  const float m_tile = mx * sl2;
+  const float m_new = fmaxf(m_run, m_tile);
+  out.need = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold || first);
+  const float m_use = out.need ? m_new : m_run;
+  const float base = (m_use == -INFINITY) ? 0.f : (m_use - kPShift);
+  out.alpha = 1.f;
+  if (out.need) out.alpha = (m_run == -INFINITY) ? 0.f : ptx::ex2(m_run - m_use);
+  m_run = m_use;
+
+  // 3 + 4. exponentials and row sum
+  const uint64_t sl2x2 = ptx::pack2(sl2, sl2);
+  const uint64_t nbx2 = ptx::pack2(-base, -base);
+  uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (int c = 0; c < NC; c += 2) {
+    const uint64_t x = ptx::ffma2(ptx::pack2(s[c], s[c + 1]), sl2x2, nbx2);
+    float x0, x1;
+    ptx::unpack2(x, x0, x1);
+    uint64_t e;
+    if ((c % 8) < kEmuPer8) {
+      e = exp2_emu_pair(x0, x1);
+      ptx::unpack2(e, s[c], s[c + 1]);
+    } else {
+      s[c] = ptx::ex2(x0);
+      s[c + 1] = ptx::ex2(x1);
+      e = ptx::pack2(s[c], s[c + 1]);
+    }
+    acc[(c / 2) % 4] = ptx::fadd2(acc[(c / 2) % 4], e);
+  }
+  {
+    const uint64_t a01 = ptx::fadd2(acc[0], acc[1]);
+    const uint64_t a23 = ptx::fadd2(acc[2], acc[3]);
+    float u0, u1;
+    ptx::unpack2(ptx::fadd2(a01, a23), u0, u1);
+    l_run = l_run * out.alpha + (u0 + u1);
+  }
+
+  // 5. e4m3 P (hi) and, for split tiles, the e4m3 residual P - hi (lo). Two
+  //    separate loops so the common (no split) path carries no branches.
+  if (!split) {
+#pragma unroll
+    for (int j = 0; j < NC / 4; ++j) {
+      ph[j] = ptx::cvt_e4m3x4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
+      pl[j] = 0u;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NC / 4; ++j) {
+      ph[j] = ptx::cvt_e4m3x4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
+      const uint32_t h01 = ptx::cvt_e4m3x2_to_f16x2((uint16_t)(ph[j] & 0xffffu));
+      const uint32_t h23 = ptx::cvt_e4m3x2_to_f16x2((uint16_t)(ph[j] >> 16));
+      const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+      const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+      pl[j] = ptx::cvt_e4m3x4(s[4 * j] - f01.x, s[4 * j + 1] - f01.y, s[4 * j + 2] - f23.x,
+                              s[4 * j + 3] - f23.y);
+    }
+  }
+  return out;
+}
+
+}  // namespace fa8

@@ -1,0 +1,100 @@
+"""GPU parity straight through the C ABI (libfa8.so via ctypes): the golden
+vectors of the reference's own naive_self_attention (test.py:8-15), the LSE
+merge kernel and the e4m3 quantiser."""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from tests import _util as U
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden" / "naive_attention_cases.npz"
+
+
+@pytest.fixture(scope="module")
+def abi(cuda):
+    from ada_cute_fp8_flash_attention_b200 import c_abi
+    return c_abi
+
+
+def fwd_cabi(abi, q, k, v_bhds, causal, scale, device, lse=False):
+    import torch
+    B, H, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    qd, kd, vd = U.to_dev(q, device), U.to_dev(k, device), U.to_dev(v_bhds, device)
+    out = torch.empty((B, H, Sq, D), dtype=torch.float16, device=device)
+    l = torch.empty((B, H, Sq), dtype=torch.float32, device=device)
+    p = abi.params(B, H, Hkv, Sq, Skv, D)
+    p.q, p.k, p.v, p.o = qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr()
+    if lse:
+        p.lse = l.data_ptr()
+    p.causal = int(causal)
+    p.softmax_scale = scale
+    abi.check(abi.fwd(p, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy(), l.cpu().numpy()
+
+
+@pytest.mark.parametrize("case", ["clamped_s128_d64", "normal_s128_d64", "normal_s256_d128"])
+@pytest.mark.parametrize("scale_name", ["sqrt_d", "sqrt_s"])
+def test_golden_reference_vectors(abi, cuda, case, scale_name):
+    g = np.load(GOLDEN)
+    q, k, v = g[case + "_q"], g[case + "_k"], g[case + "_v"]
+    key = f"{case}_{scale_name}"
+    out, _ = fwd_cabi(abi, q, k, np.ascontiguousarray(np.swapaxes(v, 2, 3)), True,
+                      float(g[key + "_scale"]), cuda)
+    U.assert_close(out, g[key + "_out"].astype(np.float32))
+
+
+def test_cabi_lse_and_offsets(abi, cuda):
+    q, k, v = U.inputs(2, 4, 2, 384, 512, 128, "normal", seed=77)
+    out, lse = fwd_cabi(abi, q, k, v, True, 1 / math.sqrt(128), cuda, lse=True)
+    o_ref, l_ref = U.oracle(q, k, v, causal=True)
+    U.assert_close(out, o_ref)
+    assert np.abs(lse - l_ref).max() < 1e-3
+
+
+def test_lse_merge_reassembles_full_attention(abi, cuda):
+    """Split the keys in 3 blocks, run each block with LSE, merge: equals one pass."""
+    import torch
+    from ada_cute_fp8_flash_attention_b200 import c_abi
+    q, k, v = U.inputs(1, 2, 2, 256, 768, 64, "normal", seed=3)
+    parts_o, parts_l = [], []
+    for j in range(3):
+        kj = np.ascontiguousarray(k[:, :, 256 * j: 256 * (j + 1)])
+        vj = np.ascontiguousarray(v[:, :, :, 256 * j: 256 * (j + 1)])
+        o, l = fwd_cabi(abi, q, kj, vj, False, 0.125, cuda, lse=True)
+        parts_o.append(torch.from_numpy(o).half().to(cuda).contiguous())
+        parts_l.append(torch.from_numpy(l).to(cuda).contiguous())
+    rows = 1 * 2 * 256
+    out = torch.empty((rows, 64), dtype=torch.float16, device=cuda)
+    lse = torch.empty(rows, dtype=torch.float32, device=cuda)
+    st = c_abi.lse_merge([t.data_ptr() for t in parts_o], 1, [t.data_ptr() for t in parts_l],
+                         rows, 64, out.data_ptr(), 64, lse.data_ptr(),
+                         torch.cuda.current_stream().cuda_stream)
+    c_abi.check(st)
+    torch.cuda.synchronize()
+    o_ref, l_ref = U.oracle(q, k, v, causal=False, scale=0.125)
+    U.assert_close(out.float().cpu().numpy().reshape(o_ref.shape), o_ref)
+    assert np.abs(lse.cpu().numpy().reshape(l_ref.shape) - l_ref).max() < 1e-3
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+def test_quantize_matches_torch_cast(abi, cuda, transpose):
+    import torch
+    x = (torch.randn(2, 3, 200, 64, device=cuda) * 40).half()
+    y = torch.empty((2, 3, 64, 200) if transpose else (2, 3, 200, 64), dtype=torch.uint8,
+                    device=cuda)
+    st = abi.quantize_e4m3(x.data_ptr(), 0, y.data_ptr(), 6, 200, 64, 1.0, transpose,
+                           torch.cuda.current_stream().cuda_stream)
+    abi.check(st)
+    torch.cuda.synchronize()
+    ref = x.float().clamp(-448, 448).to(torch.float8_e4m3fn)
+    if transpose:
+        ref = ref.transpose(-1, -2).contiguous()
+    assert torch.equal(y.cpu(), ref.view(torch.uint8).cpu())
