@@ -1,0 +1,157 @@
+"""Context-parallel (ring) causal FP8 attention over the GPUs of one node.
+
+The reference runs one sequence on one GPU only; for the long-context shape
+(S = 131072, causal) the sequence is split across W ranks:
+
+* zig-zag chunking: the sequence is cut into 2W equal chunks and rank r holds
+  chunks r and 2W-1-r of Q, K and V, so every rank owns the same amount of
+  causal work (an early chunk with few keys plus a late chunk with many);
+* ring: in step s (0 <= s < W) rank r holds the K/V chunks of rank
+  (r - s) mod W; while it runs the FP8 kernel on them (with the chunks'
+  global positions as q_offset / kv_offset, so the causal mask is exact) it
+  already sends them to rank r+1 and receives the next ones from rank r-1
+  (NCCL point-to-point over NVLink, double-buffered);
+* each (Q chunk, K/V chunk) pair yields a partial output normalised over that
+  K/V chunk and its log-sum-exp; pairs that the causal mask removes entirely
+  are skipped on the host;
+* the partials of a Q chunk are combined by log-sum-exp
+  (fa8_lse_merge: o = sum_i exp(lse_i - lse) o_i).
+
+K/V travel as e4m3 (2 x S/(2W) x D bytes per head per step); nothing is
+loaded across GPUs by the kernels themselves (no peer-memory TMA).
+
+The ring logic is written against two callables so it can be exercised on
+CPU ranks (gloo) with the oracle; the default callables are this package's
+CUDA kernels and there is no CPU fallback on the product path.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, List, Optional, Sequence, Tuple
+
+
+@dataclass(frozen=True)
+class ZigZag:
+    """Chunk bookkeeping for `world` ranks over a sequence of `seqlen` tokens."""
+
+    world: int
+    seqlen: int
+
+    @property
+    def chunk(self) -> int:
+        if self.seqlen % (2 * self.world):
+            raise ValueError("seqlen must be a multiple of 2 * world")
+        return self.seqlen // (2 * self.world)
+
+    def chunks_of(self, rank: int) -> Tuple[int, int]:
+        return rank, 2 * self.world - 1 - rank
+
+    def start(self, chunk_id: int) -> int:
+        return chunk_id * self.chunk
+
+    def visible(self, q_chunk: int, kv_chunk: int) -> bool:
+        """Does any query of q_chunk see any key of kv_chunk under the causal mask?"""
+        return kv_chunk <= q_chunk
+
+    def source_rank(self, rank: int, step: int) -> int:
+        return (rank - step) % self.world
+
+
+def split_local(x, zz: ZigZag, rank: int, dim: int):
+    """Rank `rank`'s two zig-zag chunks of a full-sequence tensor, concatenated on `dim`."""
+    import torch
+    a, b = zz.chunks_of(rank)
+    c = zz.chunk
+    return torch.cat([x.narrow(dim, a * c, c), x.narrow(dim, b * c, c)], dim=dim).contiguous()
+
+
+def gather_full(local, zz: ZigZag, group=None, dim: int = 2):
+    """Inverse of split_local across ranks (all-gather; for tests and checks)."""
+    import torch
+    import torch.distributed as dist
+    parts = [torch.empty_like(local) for _ in range(zz.world)]
+    dist.all_gather(parts, local.contiguous(), group=group)
+    c = zz.chunk
+    chunks = [None] * (2 * zz.world)
+    for r, t in enumerate(parts):
+        a, b = zz.chunks_of(r)
+        chunks[a] = t.narrow(dim, 0, c)
+        chunks[b] = t.narrow(dim, c, c)
+    return torch.cat(chunks, dim=dim)
+
+
+ComputeFn = Callable[..., Tuple[object, object]]  # (q, k, v_bhds, q_off, kv_off) -> (o, lse)
+MergeFn = Callable[[Sequence[object], Sequence[object]], Tuple[object, object]]
+
+
+def _default_compute(softmax_scale: Optional[float]):
+    from . import flash_attn_fp8_forward_ex
+
+    def compute(q, k, v_bhds, q_off, kv_off):
+        return flash_attn_fp8_forward_ex(q, k, v_bhds, causal=True, softmax_scale=softmax_scale,
+                                         v_layout="bhds", return_lse=True, q_offset=q_off,
+                                         kv_offset=kv_off)
+    return compute
+
+
+def _default_merge(outs, lses):
+    from . import lse_merge
+    return lse_merge([o.contiguous() for o in outs], [l.contiguous() for l in lses])
+
+
+def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
+                   softmax_scale: Optional[float] = None,
+                   compute: Optional[ComputeFn] = None, merge: Optional[MergeFn] = None):
+    """Causal attention of this rank's zig-zag Q chunks against the whole sequence.
+
+    q_loc, k_loc: (B, H, 2*chunk, D) e4m3 — this rank's chunks (split_local, dim 2);
+    v_loc_bhds: (B, H, D, 2*chunk) e4m3 — V^T chunks (split_local, dim 3).
+    Returns (o_loc, lse_loc) for the local Q chunks in the same layout as q_loc.
+    """
+    import torch
+    import torch.distributed as dist
+
+    compute = compute or _default_compute(softmax_scale)
+    merge = merge or _default_merge
+    W, c = zz.world, zz.chunk
+    my_chunks = zz.chunks_of(rank)
+    q_parts = [q_loc.narrow(2, 0, c), q_loc.narrow(2, c, c)]
+    partial_o: List[list] = [[], []]
+    partial_l: List[list] = [[], []]
+
+    cur_k, cur_v = k_loc.contiguous(), v_loc_bhds.contiguous()
+    nxt_k, nxt_v = torch.empty_like(cur_k), torch.empty_like(cur_v)
+    send_to, recv_from = (rank + 1) % W, (rank - 1) % W
+    for step in range(W):
+        reqs = []
+        if step + 1 < W:
+            # Start passing the current block on before computing with it.
+            # e4m3 blocks travel as raw bytes.
+            u8 = lambda t: t.view(torch.uint8)  # noqa: E731
+            ops = [dist.P2POp(dist.isend, u8(cur_k), send_to, group),
+                   dist.P2POp(dist.isend, u8(cur_v), send_to, group),
+                   dist.P2POp(dist.irecv, u8(nxt_k), recv_from, group),
+                   dist.P2POp(dist.irecv, u8(nxt_v), recv_from, group)]
+            reqs = dist.batch_isend_irecv(ops)
+        src = zz.source_rank(rank, step)
+        kv_chunks = zz.chunks_of(src)
+        for qi, qc in enumerate(my_chunks):
+            for kj, kc in enumerate(kv_chunks):
+                if not zz.visible(qc, kc):
+                    continue
+                k_blk = cur_k.narrow(2, kj * c, c)
+                v_blk = cur_v.narrow(3, kj * c, c)
+                o, l = compute(q_parts[qi], k_blk, v_blk, zz.start(qc), zz.start(kc))
+                partial_o[qi].append(o)
+                partial_l[qi].append(l)
+        for r in reqs:
+            r.wait()
+        if step + 1 < W:
+            cur_k, nxt_k = nxt_k, cur_k
+            cur_v, nxt_v = nxt_v, cur_v
+    outs, lses = [], []
+    for qi in range(2):
+        o, l = merge(partial_o[qi], partial_l[qi])
+        outs.append(o)
+        lses.append(l)
+    return torch.cat(outs, dim=2), torch.cat(lses, dim=2)
