@@ -35,8 +35,22 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-WORKLOAD = dict(name="C2", batch=4, heads=32, seqlen=4096, head_dim=128, causal=False,
-                dist="normal", sigma=1.0, seed=1234)
+# C2 is the headline (default); the others are available
+# through --workload for the per-config table (C5 is context parallel).
+CONFIGS = {
+    "c1": dict(name="C1 B1 H8 S512 D64 non-causal N(0,1) (BASELINE configs[0])", batch=1,
+               heads=8, seqlen=512, head_dim=64, causal=False, dist="normal", sigma=1.0),
+    "c2": dict(name="C2 B4 H32 S4096 D128 non-causal N(0,1) (BASELINE configs[1])", batch=4,
+               heads=32, seqlen=4096, head_dim=128, causal=False, dist="normal", sigma=1.0),
+    "c3": dict(name="C3 B8 H32 S8192 D128 causal 0.5*N(0,1) (BASELINE configs[2])", batch=8,
+               heads=32, seqlen=8192, head_dim=128, causal=True, dist="normal", sigma=0.5),
+    "c4": dict(name="C4 B64 H16 S1024 D64 non-causal U[-2,2] (BASELINE configs[3])", batch=64,
+               heads=16, seqlen=1024, head_dim=64, causal=False, dist="uniform", sigma=1.0),
+    "c5": dict(name="C5 B1 H32 S131072 D128 causal N(0,1), context parallel "
+               "(BASELINE configs[4])", batch=1, heads=32, seqlen=131072, head_dim=128,
+               causal=True, dist="normal", sigma=1.0),
+}
+WORKLOAD = dict(CONFIGS["c2"], seed=1234)
 METRIC = "FP8 attn fwd TFLOPS/GPU and % of FP8 dense peak; ms/call at 1/2/4/8 B200"
 FP8_SPEC_TFLOPS = 4500.0
 
@@ -149,10 +163,14 @@ def make_inputs_dev(device, rank):
     gen = torch.Generator(device="cpu").manual_seed(seed)
     # Drawn on the host (the e2e arm copies them from pinned memory), cast to
     # e4m3 with scale 1.0 (round to nearest even).
-    q = (torch.randn((B, H, S, D), generator=gen) * W["sigma"]).to(torch.float8_e4m3fn)
-    k = (torch.randn((B, H, S, D), generator=gen) * W["sigma"]).to(torch.float8_e4m3fn)
-    v = (torch.randn((B, H, D, S), generator=gen) * W["sigma"]).to(torch.float8_e4m3fn)
-    return q, k, v
+    def draw(shape):
+        if W["dist"] == "uniform":
+            x = torch.rand(shape, generator=gen) * 4.0 - 2.0
+        else:
+            x = torch.randn(shape, generator=gen) * W["sigma"]
+        return x.to(torch.float8_e4m3fn)
+
+    return draw((B, H, S, D)), draw((B, H, S, D)), draw((B, H, D, S))
 
 
 def fp8_gemm_probe(device):
@@ -230,9 +248,9 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total_flops / (v * 1e12) * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "C2 B4 H32 S4096 D128 non-causal (BASELINE configs[1])",
+        "config": {"workload": W["name"],
                    "global_batch": W["batch"], "seq_len": W["seqlen"], "heads": W["heads"],
-                   "head_dim": W["head_dim"], "causal": False,
+                   "head_dim": W["head_dim"], "causal": W["causal"],
                    "path": "test.py:8-15 naive attention, fp32 numpy on host cores "
                            "(oracle/attention_ref.py)"},
         "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": cores, "kind": "port",
@@ -334,8 +352,8 @@ def run_framework(args):
     if rank == 0 and world == 1 and not args.no_cpu:
         tf, units, el = cpu_baseline_sample(max_seconds=args.cpu_seconds)
         cpu = {"value": tf, "unit": "TFLOPS", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{units} (batch, head) units of the workload (S=4096, D=128, "
-                         f"non-causal) in {el:.1f}s, test.py:8-15 math in fp32 numpy"}
+               "sample": f"{units} (batch, head) units of the workload (S={S}, D={D}, "
+                         f"causal={causal}) in {el:.1f}s, test.py:8-15 math in fp32 numpy"}
 
     if rank == 0:
         hbm, bf16, src = load_peaks()
@@ -346,11 +364,12 @@ def run_framework(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "e4m3", "data": "synthetic",
-            "config": {"workload": "C2 B4 H32 S4096 D128 non-causal (BASELINE configs[1]), "
-                                   "per GPU", "global_batch": B * world, "seq_len": S,
+            "config": {"workload": W["name"] + ", per GPU", "global_batch": B * world,
+                       "seq_len": S,
                        "heads": H, "head_dim": D, "causal": causal,
                        "parallelism": f"dp{world} over (batch, head), no collective",
-                       "l2": "inputs larger than L2 (Q/K/V 192 MiB + O 128 MiB per GPU)"},
+                       "l2": ("inputs larger than L2" if algo_bytes(B, H, S, S, D) > 126e6
+                              else "inputs fit in L2; consecutive steps reuse them")},
             "tflops_per_gpu": value / world,
             "pct_fp8_spec_peak": 100.0 * value / world / FP8_SPEC_TFLOPS,
             "pct_fp8_2x_measured_bf16": 100.0 * value / world / fp8_peak,
@@ -378,6 +397,74 @@ def run_framework(args):
     return 0
 
 
+def run_context_parallel(args):
+    """C5: one causal sequence of 131072 tokens split over all ranks (zig-zag ring)."""
+    import torch
+
+    world, rank, local = dist_setup(args)
+    device = torch.device("cuda", local)
+    import torch.distributed as dist
+    import ada_cute_fp8_flash_attention_b200 as fa8
+    from ada_cute_fp8_flash_attention_b200 import context_parallel as cp
+
+    W = WORKLOAD
+    B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
+    zz = cp.ZigZag(world, S)
+    c = zz.chunk
+    gen = torch.Generator(device="cpu").manual_seed(W["seed"])
+    # Each rank draws only its own chunks (seeded per chunk id).
+    def chunk(shape_fn, salt):
+        parts = []
+        for cid in zz.chunks_of(rank):
+            g = torch.Generator(device="cpu").manual_seed(W["seed"] + 7919 * cid + salt)
+            parts.append((torch.randn(shape_fn(), generator=g) * W["sigma"]).to(torch.float8_e4m3fn))
+        return parts
+    ql = torch.cat(chunk(lambda: (B, H, c, D), 1), dim=2).to(device)
+    kl = torch.cat(chunk(lambda: (B, H, c, D), 2), dim=2).to(device)
+    vl = torch.cat(chunk(lambda: (B, H, D, c), 3), dim=3).to(device)
+    del gen
+    step = lambda: cp.ring_attention(ql, kl, vl, zz, rank)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier() if world > 1 else None
+    launches0 = fa8.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total = flops(B, H, S, S, D, True)
+    value = total / (ms * 1e-3) / 1e12
+    if rank == 0:
+        hbm, bf16, src = load_peaks()
+        line = {"metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "e4m3", "data": "synthetic",
+                "config": {"workload": W["name"], "global_batch": B, "seq_len": S,
+                           "heads": H, "head_dim": D, "causal": True,
+                           "parallelism": f"cp{world} zig-zag ring (NCCL send/recv) + LSE merge"},
+                "tflops_per_gpu": value / world,
+                "pct_fp8_spec_peak": 100.0 * value / world / FP8_SPEC_TFLOPS,
+                "pct_fp8_2x_measured_bf16": 100.0 * value / world / (2 * bf16),
+                "gpu_launches": fa8.launch_count() - launches0,
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -387,9 +474,11 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e arm")
+    ap.add_argument("--workload", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--shape", default=None,
                     help="B,H,S,D,causal override for profiling runs (not a bench line)")
     args = ap.parse_args()
+    WORKLOAD.update(CONFIGS[args.workload])
     if args.shape:
         b, h, s, d, c = args.shape.split(",")
         WORKLOAD.update(batch=int(b), heads=int(h), seqlen=int(s), head_dim=int(d),
@@ -398,6 +487,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "c5":
+        return run_context_parallel(args)
     return run_framework(args)
 
 
