@@ -75,6 +75,9 @@ constexpr int kEmuPer8 = FA8_EMU;
 #define FA8_STAGGER 1
 #endif
 constexpr bool kStagger = FA8_STAGGER != 0;
+#ifndef FA8_WAIT_SLEEP
+#define FA8_WAIT_SLEEP 20000  // suspend-time hint (ns) of mbarrier waits; 0 = spin
+#endif
 constexpr long long kTimeoutCycles = 4000000000LL;
 constexpr int kDefaultSplitKeys = 1024;
 
@@ -152,14 +155,18 @@ struct Bars {
 // Bounded wait on phase `parity` of `bar`. Returns false on abort/timeout.
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
                                              volatile int* abort_flag, int* status) {
-#pragma unroll 1
-  for (int spin = 0; spin < 64; ++spin)
-    if (ptx::mbar_try_wait(bar, parity)) return true;
+  if (ptx::mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
+#if FA8_WAIT_SLEEP
+    // Suspends until the phase completes (or the hint expires): a waiting warp
+    // takes no issue slots from the warps that share its scheduler.
+    if (ptx::mbar_try_wait_sleep(bar, parity, FA8_WAIT_SLEEP)) return true;
+#else
 #pragma unroll 1
     for (int spin = 0; spin < 64; ++spin)
       if (ptx::mbar_try_wait(bar, parity)) return true;
+#endif
     if (*abort_flag) return false;
     if (clock64() - t0 > kTimeoutCycles) {
       *abort_flag = 1;
@@ -251,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fa8_trace_cta[cta_lin][2] = smid;
   }
 #endif
+  if (threadIdx.x == 0) FA8_TR(2, 63, 0);
   const int qb = p.causal ? (p.n_qblocks - 1 - (int)blockIdx.x) : (int)blockIdx.x;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
@@ -314,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
   volatile int* abort_flag = &abort_sh;
+  if (threadIdx.x == 0) FA8_TR(2, 63, 1);
 
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ TMA producer
@@ -515,8 +524,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = bounded_wait(&bars.offset, 0, abort_flag, p.status);
         if (!ok) break;
       }
+#ifndef FA8_SPLIT_TEMPLATE
+#define FA8_SPLIT_TEMPLATE 1
+#endif
+#if FA8_SPLIT_TEMPLATE
+      // Two specialised copies: the common path carries no split code at all.
+      const StepOut so =
+          split ? softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, true, m_run, l_run, ph, pl)
+                : softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, false, m_run, l_run, ph,
+                                                      pl);
+#else
       const StepOut so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, split, m_run,
                                                              l_run, ph, pl);
+#endif
       if (kStagger && i == 0 && tl == 0) {
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars.offset);
@@ -570,7 +590,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) ptx::mbar_arrive(&bars.offset);
     }
     // Epilogue: O / l -> global, LSE.
+    if (r == 0) FA8_TR(i, 63, 0);
     if (n > 0 && ok) ok = bounded_wait(&bars.o_done[i], (n - 1) & 1, abort_flag, p.status);
+    if (r == 0) FA8_TR(i, 63, 1);
     if (tp[i].q_start < p.seqlen_q) {
       ptx::tc_fence_after();
       const float inv_l = (l_run > 0.f && ok) ? 1.f / l_run : 0.f;
@@ -599,8 +621,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (warp < 8 && threadIdx.x % kBlockM == 0) FA8_TR(warp / 4, 63, 2);
   ptx::tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) FA8_TR(2, 63, 2);
   if (warp == kMmaWarp) {
     __syncwarp();
     ptx::tc_fence_after();
