@@ -75,6 +75,12 @@ constexpr int kEmuPer8 = FA8_EMU;
 #define FA8_STAGGER 1
 #endif
 constexpr bool kStagger = FA8_STAGGER != 0;
+#ifndef FA8_REGS_CONTROL
+#define FA8_REGS_CONTROL 104  // 0 = no register reallocation
+#define FA8_REGS_SOFTMAX 200
+#endif
+static_assert(FA8_REGS_CONTROL == 0 || 128 * FA8_REGS_CONTROL + 256 * FA8_REGS_SOFTMAX <= 384 * 168,
+              "setmaxnreg split exceeds the launch register budget");
 #ifndef FA8_WAIT_SLEEP
 #define FA8_WAIT_SLEEP 20000  // suspend-time hint (ns) of mbarrier waits; 0 = spin
 #endif
@@ -323,7 +329,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_base_sh;
   volatile int* abort_flag = &abort_sh;
   if (threadIdx.x == 0) FA8_TR(2, 63, 1);
+  // With FA8_REGS_CONTROL set, registers move from the control warpgroup
+  // (TMA / MMA issue) to the two softmax warpgroups; the setmaxnreg sits at
+  // the top of each role's branch so the compiler sees one budget per role.
+  // 128 x FA8_REGS_CONTROL + 256 x FA8_REGS_SOFTMAX must not exceed the
+  // 384 x 168 registers the CTA was launched with.
+#if FA8_REGS_CONTROL
+#define FA8_REGS_DEC() asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(FA8_REGS_CONTROL))
+#define FA8_REGS_INC() asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(FA8_REGS_SOFTMAX))
+#else
+#define FA8_REGS_DEC() do {} while (0)
+#define FA8_REGS_INC() do {} while (0)
+#endif
 
+  if (warp >= 8) {
+  FA8_REGS_DEC();
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -462,7 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (!ptx::mbar_try_wait(&bars.drain[i], 0) && clock64() - t0 < kTimeoutCycles) {
       }
     }
-  } else if (warp < 8) {
+  }
+  } else {
+    FA8_REGS_INC();
     // ------------------------------------------------------------ softmax WGs
     const int i = warp / 4;                 // query tile of this warpgroup
     const int r = threadIdx.x % kBlockM;    // row within the tile == TMEM lane
