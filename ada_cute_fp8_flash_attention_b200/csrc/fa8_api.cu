@@ -18,6 +18,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -74,15 +75,15 @@ int make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t row
   return FA8_OK;
 }
 
-template <int D>
+template <int D, int T>
 int setup_kernel_attr(int dev) {
   static std::once_flag flags[64];
   static cudaError_t errs[64];
   if (dev < 0 || dev >= 64) return set_msg(FA8_ERR_INVALID_ARG, "device index out of range");
   std::call_once(flags[dev], [dev] {
-    errs[dev] = cudaFuncSetAttribute(fa8::fa8_fwd_kernel<D>,
+    errs[dev] = cudaFuncSetAttribute(fa8::fa8_fwd_kernel<D, T>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     fa8::TileCfg<D>::kSmemAlloc);
+                                     fa8::TileCfg<D, T>::kSmemAlloc);
   });
   if (errs[dev] != cudaSuccess) return set_cuda_error(errs[dev], "cudaFuncSetAttribute");
   return FA8_OK;
@@ -90,10 +91,10 @@ int setup_kernel_attr(int dev) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <int D>
+template <int D, int T>
 int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
-  using C = fa8::TileCfg<D>;
-  int st = setup_kernel_attr<D>(dev);
+  using C = fa8::TileCfg<D, T>;
+  int st = setup_kernel_attr<D, T>(dev);
   if (st) return st;
   const CUtensorMapSwizzle swz_qk =
       (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -121,7 +122,7 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.causal = p->causal ? 1 : 0;
   kp.out_e4m3 = p->out_dtype == FA8_OUT_E4M3 ? 1 : 0;
   kp.split_keys = p->split_keys < 0 ? fa8::kDefaultSplitKeys : p->split_keys;
-  const int rows_per_cta = fa8::kTilesPerCta * fa8::kBlockM;
+  const int rows_per_cta = T * fa8::kBlockM;
   kp.n_qblocks = (int)((p->seqlen_q + rows_per_cta - 1) / rows_per_cta);
   kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
   kp.q_offset = p->q_offset;
@@ -136,7 +137,7 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.status = p->status;
 
   dim3 grid(kp.n_qblocks, (unsigned)p->heads, (unsigned)p->batch);
-  fa8::fa8_fwd_kernel<D><<<grid, fa8::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, kp);
+  fa8::fa8_fwd_kernel<D, T><<<grid, fa8::Roles<T>::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, kp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "fa8_fwd_kernel launch");
@@ -224,7 +225,15 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
     return set_msg(FA8_ERR_NO_DEVICE, "the current device is not sm_100 (B200)");
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return p->head_dim == 128 ? launch<128>(p, s, dev) : launch<64>(p, s, dev);
+  // Query tiles per CTA: 1 (two CTAs per SM, measured faster on every
+  // configuration) unless FA8_TILES=2 is set in the environment.
+  static int tiles_env = [] {
+    const char* e = getenv("FA8_TILES");
+    return e ? atoi(e) : 0;
+  }();
+  const int tiles = (tiles_env == 1 || tiles_env == 2) ? tiles_env : 1;
+  if (p->head_dim == 128) return tiles == 1 ? launch<128, 1>(p, s, dev) : launch<128, 2>(p, s, dev);
+  return tiles == 1 ? launch<64, 1>(p, s, dev) : launch<64, 2>(p, s, dev);
 }
 
 const char* fa8_status_string(int status) {

@@ -5,16 +5,17 @@
 // (csrc/flash_attention.cu:90-460) and its traits (csrc/kernel_traits.h:11-87)
 // with a Blackwell design:
 //
-//   * one CTA owns two 128-row query tiles (Q0, Q1) of one (batch, head);
-//   * 384 threads = three warpgroups; warp 11 of the control warpgroup is
-//     idle;
-//   * warp 9 (TMA) streams K and V tiles (128 keys each) into a ring of
+//   * a CTA owns T = 1 (default; two CTAs per SM) or T = 2 (one CTA per SM)
+//     128-row query tiles of one (batch, head); 128 (T + 1) threads: T softmax
+//     warpgroups and one control warpgroup; setmaxnreg gives the softmax
+//     warpgroups 200 registers per thread;
+//   * control warp 1 (TMA) streams K and V tiles (128 keys each) into a ring of
 //     shared-memory stages (cp.async.bulk.tensor, mbarrier completion);
-//   * warps 8 and 10 (one elected thread each, one per query tile) issue
-//     tcgen05.mma kind::f8f6f4:
+//   * control warps 0 and 2 (one elected thread each, one per query tile)
+//     issue tcgen05.mma kind::f8f6f4:
 //       S_i = Q_i K^T  into TMEM (128 lanes x 128 f32 columns per tile),
 //       O_i += P_i V   into TMEM (128 lanes x D f32 columns per tile);
-//   * warps 0-3 and 4-7 are the softmax warpgroups of Q0 and Q1. Each thread
+//   * warps 0-3 (and 4-7) are the softmax warpgroups of Q0 (and Q1). Each thread
 //     owns one query row (one TMEM lane): row max and row sum need no
 //     shuffles. They run the online softmax in base 2 (the reference's
 //     softmax_rescale_o, csrc/flash_attention.cu:54-88, with the scale fixed
@@ -57,13 +58,30 @@
 
 namespace fa8 {
 
-constexpr int kThreads = 384;          // 2 softmax warpgroups + 1 control warpgroup
 constexpr int kBlockM = 128;           // query rows per tile (= TMEM lanes)
 constexpr int kBlockN = 128;           // keys per K/V tile
-constexpr int kTilesPerCta = 2;        // query tiles per CTA
-constexpr int kMmaWarp = 8;
-constexpr int kLoadWarp = 9;
-constexpr int kMmaWarp2 = 10;
+// A CTA owns T query tiles (T = 2: one CTA per SM; T = 1: two CTAs per SM,
+// whose prologues / epilogues overlap each other's main loops). Warps 0..4T-1
+// are the softmax warpgroups; the control warpgroup follows: its warp 0
+// issues tile 0's MMAs, warp 1 is the TMA producer, warp 2 issues tile 1's.
+template <int T>
+struct Roles {
+  static_assert(T == 1 || T == 2, "one or two query tiles per CTA");
+  static constexpr int kThreads = 128 * (T + 1);
+  static constexpr int kCtrl = 4 * T;
+  static constexpr int kMmaWarp = kCtrl;
+  static constexpr int kLoadWarp = kCtrl + 1;
+  static constexpr int kMmaWarp2 = kCtrl + 2;
+  static constexpr int kMinBlocks = (T == 1) ? 2 : 1;
+  // setmaxnreg budgets: control + softmax registers must fit the launch budget
+  // (65536 / kMinBlocks per CTA), and per scheduler 2 softmax warps + 1
+  // control warp (x kMinBlocks CTAs) must fit its 512 registers per lane.
+  static constexpr int kRegsControl = (T == 1) ? 56 : 104;
+  static constexpr int kRegsSoftmax = 200;
+  static_assert(128 * kRegsControl + 128 * T * kRegsSoftmax <=
+                    (65536 / kMinBlocks / (128 * (T + 1))) / 8 * 8 * 128 * (T + 1),
+                "setmaxnreg split exceeds the launch register budget");
+};
 #ifndef FA8_EMU
 #define FA8_EMU 0
 #endif
@@ -76,18 +94,15 @@ constexpr int kEmuPer8 = FA8_EMU;
 #endif
 constexpr bool kStagger = FA8_STAGGER != 0;
 #ifndef FA8_REGS_CONTROL
-#define FA8_REGS_CONTROL 104  // 0 = no register reallocation
-#define FA8_REGS_SOFTMAX 200
+#define FA8_REGS_CONTROL 1  // 0 = no register reallocation between roles
 #endif
-static_assert(FA8_REGS_CONTROL == 0 || 128 * FA8_REGS_CONTROL + 256 * FA8_REGS_SOFTMAX <= 384 * 168,
-              "setmaxnreg split exceeds the launch register budget");
 #ifndef FA8_WAIT_SLEEP
 #define FA8_WAIT_SLEEP 20000  // suspend-time hint (ns) of mbarrier waits; 0 = spin
 #endif
 constexpr long long kTimeoutCycles = 4000000000LL;
 constexpr int kDefaultSplitKeys = 1024;
 
-template <int D>
+template <int D, int T>
 struct TileCfg {
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
   static constexpr int kQKRowBytes = D;                  // e4m3 rows of Q and K
@@ -95,17 +110,17 @@ struct TileCfg {
   static constexpr int kKBytes = kBlockN * D;
   static constexpr int kVBytes = D * kBlockN;            // V^T tile: D rows of 128 keys
   static constexpr int kStageBytes = kKBytes;            // == kVBytes
-  static constexpr int kStages = (D == 128) ? 6 : 8;
+  static constexpr int kStages = (T == 2) ? ((D == 128) ? 6 : 8) : ((D == 128) ? 3 : 8);
   static constexpr int kPBytes = kBlockM * kBlockN;      // 128 rows x 128 B
   static constexpr int kOffQ = 0;
-  static constexpr int kOffRing = kTilesPerCta * kQBytes;
+  static constexpr int kOffRing = T * kQBytes;
   static constexpr int kOffP = kOffRing + kStages * kStageBytes;
-  static constexpr int kSmemBytes = kOffP + 2 * kTilesPerCta * kPBytes;  // hi + lo per tile
+  static constexpr int kSmemBytes = kOffP + 2 * T * kPBytes;  // hi + lo per tile
   static constexpr int kSmemAlloc = kSmemBytes + 1024;   // slack for 1024-B alignment
-  // TMEM columns: S0 | S1 | O0 | O1
+  // TMEM columns: S0 | S1 | O0 | O1 (T = 2) or S0 | O0 (T = 1)
   static constexpr uint32_t kColS = 0;
-  static constexpr uint32_t kColO = kTilesPerCta * kBlockN;
-  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColO = T * kBlockN;
+  static constexpr uint32_t kTmemCols = (T == 2) ? 512 : 256;
   static constexpr uint32_t kIdescS = ptx::idesc_e4m3_f32(kBlockM, kBlockN);
   static constexpr uint32_t kIdescO = ptx::idesc_e4m3_f32(kBlockM, D);
 };
@@ -145,7 +160,7 @@ __device__ __forceinline__ long long fa8_gtimer() {
 #endif
 
 // Barrier slots in static shared memory.
-template <int NS>
+template <int NS, int kTilesPerCta>
 struct Bars {
   uint64_t q_full[kTilesPerCta];
   uint64_t kv_full[NS];
@@ -189,6 +204,7 @@ struct TilePlan {
   int q_start; // first query row (local)
 };
 
+template <int kTilesPerCta>
 __device__ __forceinline__ TilePlan plan_tile(const KernelParams& p, int qb, int i) {
   TilePlan t;
   t.q_start = qb * (kTilesPerCta * kBlockM) + i * kBlockM;
@@ -242,14 +258,20 @@ __device__ __forceinline__ void store_o_chunk(const KernelParams& p, char* row_p
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, int kTilesPerCta>
+__global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPerCta>::kMinBlocks)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const KernelParams p) {
-  using C = TileCfg<D>;
+  using C = TileCfg<D, kTilesPerCta>;
+  using R = Roles<kTilesPerCta>;
+  constexpr int kMmaWarp = R::kMmaWarp;
+  constexpr int kLoadWarp = R::kLoadWarp;
+  constexpr int kMmaWarp2 = R::kMmaWarp2;
+  constexpr int kSoftmaxWarps = 4 * kTilesPerCta;
+  constexpr bool kStaggerT = kStagger && kTilesPerCta == 2;
   constexpr int NS = C::kStages;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ Bars<NS> bars;
+  __shared__ Bars<NS, kTilesPerCta> bars;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -272,8 +294,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   TilePlan tp[kTilesPerCta];
 #pragma unroll
-  for (int i = 0; i < kTilesPerCta; ++i) tp[i] = plan_tile(p, qb, i);
-  const int nmax = max(tp[0].n, tp[1].n);
+  for (int i = 0; i < kTilesPerCta; ++i) tp[i] = plan_tile<kTilesPerCta>(p, qb, i);
+  int nmax = 0;
+#pragma unroll
+  for (int i = 0; i < kTilesPerCta; ++i) nmax = max(nmax, tp[i].n);
 
   char* o_head = reinterpret_cast<char*>(p.o) +
                  ((long long)b * p.o_sb + (long long)h * p.o_sh) * (p.out_e4m3 ? 1 : 2);
@@ -281,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (nmax == 0) {
     // Every row of this CTA is fully masked: O = 0, LSE = -inf.
-    if (warp < 8) {
+    if (warp < kSoftmaxWarps) {
       const int i = warp / 4;
       const int row = tp[i].q_start + (threadIdx.x % kBlockM);
       if (tp[i].q_start < p.seqlen_q && row < p.seqlen_q) {
@@ -335,14 +359,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   // 128 x FA8_REGS_CONTROL + 256 x FA8_REGS_SOFTMAX must not exceed the
   // 384 x 168 registers the CTA was launched with.
 #if FA8_REGS_CONTROL
-#define FA8_REGS_DEC() asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(FA8_REGS_CONTROL))
-#define FA8_REGS_INC() asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(FA8_REGS_SOFTMAX))
+#define FA8_REGS_DEC() asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R::kRegsControl))
+#define FA8_REGS_INC() asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R::kRegsSoftmax))
 #else
 #define FA8_REGS_DEC() do {} while (0)
 #define FA8_REGS_INC() do {} while (0)
 #endif
 
-  if (warp >= 8) {
+  if (warp >= kSoftmaxWarps) {
   FA8_REGS_DEC();
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ TMA producer
@@ -393,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == kMmaWarp || warp == kMmaWarp2) {
+  } else if (warp == kMmaWarp || (kTilesPerCta == 2 && warp == kMmaWarp2)) {
     // ------------------------------------------------------------ MMA issuers
     // One issuing thread per query tile (warp 8: Q0, warp 10: Q1), so each
     // tile's QK -> softmax -> PV chain advances at its own pace; the two
@@ -403,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i = (warp == kMmaWarp) ? 0 : 1;
       const uint32_t q_addr = s_base + C::kOffQ + i * C::kQBytes;
       const uint32_t p_hi = s_base + C::kOffP + i * C::kPBytes;
-      const uint32_t p_lo = s_base + C::kOffP + (2 + i) * C::kPBytes;
+      const uint32_t p_lo = s_base + C::kOffP + (kTilesPerCta + i) * C::kPBytes;
       const int start = nmax - tp[i].n;
       const bool active = tp[i].n > 0;
       const int role = 2 + i;
@@ -492,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t t_s = tmem + lane_off + C::kColS + i * kBlockN;
     const uint32_t t_o = tmem + lane_off + C::kColO + i * D;
     const uint32_t p_hi = s_base + C::kOffP + i * C::kPBytes;
-    const uint32_t p_lo = s_base + C::kOffP + (2 + i) * C::kPBytes;
+    const uint32_t p_lo = s_base + C::kOffP + (kTilesPerCta + i) * C::kPBytes;
     const int n = tp[i].n;
     const int row = tp[i].q_start + r;  // local query row
     const long long row_g = p.q_offset + row;
@@ -540,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph[kBlockN / 4];
       uint32_t pl[kBlockN / 4];
       const bool split = tp[i].split != 0;
-      if (kStagger && i == 1 && tl == 0) {
+      if (kStaggerT && i == 1 && tl == 0) {
         // Start one exp phase behind warpgroup 0 so that one group's barrier
         // waits, S loads and P stores overlap the other's exp work.
         ok = bounded_wait(&bars.offset, 0, abort_flag, p.status);
@@ -559,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const StepOut so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, split, m_run,
                                                              l_run, ph, pl);
 #endif
-      if (kStagger && i == 0 && tl == 0) {
+      if (kStaggerT && i == 0 && tl == 0) {
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars.offset);
         offset_sent = true;
@@ -607,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (r == 0) FA8_TR(i, tl, 5);
     }
 
-    if (kStagger && i == 0 && !offset_sent) {
+    if (kStaggerT && i == 0 && !offset_sent) {
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars.offset);
     }
@@ -643,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (warp < 8 && threadIdx.x % kBlockM == 0) FA8_TR(warp / 4, 63, 2);
+  if (warp < kSoftmaxWarps && threadIdx.x % kBlockM == 0) FA8_TR(warp / 4, 63, 2);
   ptx::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) FA8_TR(2, 63, 2);
