@@ -551,16 +551,12 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       if (lane == 0) ptx::mbar_arrive(&bars.s_free[i]);
       if (r == 0) FA8_TR(i, tl, 2);
 
-      // Mask: keys past seqlen_kv, and (causal) keys after this query.
+      // Does any row of this tile need masking at this K/V tile? (keys past
+      // seqlen_kv, or, causal, keys after the tile's first query)
       const int kv0 = kv * kBlockN;
-      long long lim = p.seqlen_kv - kv0;
-      if (p.causal) lim = min(lim, row_g - p.kv_offset - kv0 + 1);
-      if (lim < kBlockN) {
-        const int li = (int)max(lim, -1LL);
-#pragma unroll
-        for (int c = 0; c < kBlockN; ++c)
-          if (c >= li) s[c] = -INFINITY;
-      }
+      const bool tile_masked =
+          (kv0 + kBlockN > p.seqlen_kv) ||
+          (p.causal && p.kv_offset + kv0 + kBlockN - 1 > p.q_offset + tp[i].q_start);
       uint32_t ph[kBlockN / 4];
       uint32_t pl[kBlockN / 4];
       const bool split = tp[i].split != 0;
@@ -570,19 +566,22 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         ok = bounded_wait(&bars.offset, 0, abort_flag, p.status);
         if (!ok) break;
       }
-#ifndef FA8_SPLIT_TEMPLATE
-#define FA8_SPLIT_TEMPLATE 1
-#endif
-#if FA8_SPLIT_TEMPLATE
-      // Two specialised copies: the common path carries no split code at all.
-      const StepOut so =
-          split ? softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, true, m_run, l_run, ph, pl)
-                : softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, false, m_run, l_run, ph,
-                                                      pl);
-#else
-      const StepOut so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, split, m_run,
-                                                             l_run, ph, pl);
-#endif
+      StepOut so;
+      if (!tile_masked && !split) {
+        // Hot path: an unmasked K/V tile, single-term P — no mask or split code.
+        so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, false, m_run, l_run, ph, pl);
+      } else {
+        // Mask: keys past seqlen_kv, and (causal) keys after this query.
+        long long lim = p.seqlen_kv - kv0;
+        if (p.causal) lim = min(lim, row_g - p.kv_offset - kv0 + 1);
+        if (lim < kBlockN) {
+          const int li = (int)max(lim, -1LL);
+#pragma unroll
+          for (int c = 0; c < kBlockN; ++c)
+            if (c >= li) s[c] = -INFINITY;
+        }
+        so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, split, m_run, l_run, ph, pl);
+      }
       if (kStaggerT && i == 0 && tl == 0) {
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars.offset);
