@@ -6,11 +6,12 @@ The reference runs one sequence on one GPU only; for the long-context shape
 * zig-zag chunking: the sequence is cut into 2W equal chunks and rank r holds
   chunks r and 2W-1-r of Q, K and V, so every rank owns the same amount of
   causal work (an early chunk with few keys plus a late chunk with many);
-* ring: in step s (0 <= s < W) rank r holds the K/V chunks of rank
-  (r - s) mod W; while it runs the FP8 kernel on them (with the chunks'
-  global positions as q_offset / kv_offset, so the causal mask is exact) it
-  already sends them to rank r+1 and receives the next ones from rank r-1
-  (NCCL point-to-point over NVLink, double-buffered);
+* K/V exchange, two schedules: "allgather" (default) gathers every rank's
+  e4m3 K/V chunks with one asynchronous NCCL all-gather while the rank's own
+  chunk pairs run; "ring" passes them in W steps, rank r -> r+1 (NCCL
+  point-to-point over NVLink, double-buffered), overlapped with the kernel.
+  Either way the kernel gets the chunks' global positions as q_offset /
+  kv_offset, so the causal mask is exact;
 * each (Q chunk, K/V chunk) pair yields a partial output normalised over that
   K/V chunk and its log-sum-exp; pairs that the causal mask removes entirely
   are skipped on the host;
@@ -101,18 +102,30 @@ def _default_merge(outs, lses):
 
 def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
                    softmax_scale: Optional[float] = None,
-                   compute: Optional[ComputeFn] = None, merge: Optional[MergeFn] = None):
+                   compute: Optional[ComputeFn] = None, merge: Optional[MergeFn] = None,
+                   schedule: str = "allgather"):
     """Causal attention of this rank's zig-zag Q chunks against the whole sequence.
 
     q_loc, k_loc: (B, H, 2*chunk, D) e4m3 — this rank's chunks (split_local, dim 2);
     v_loc_bhds: (B, H, D, 2*chunk) e4m3 — V^T chunks (split_local, dim 3).
     Returns (o_loc, lse_loc) for the local Q chunks in the same layout as q_loc.
+
+    schedule "ring": W steps of point-to-point K/V passing overlapped with the
+    kernel; "allgather" (default): one all-gather of every rank's K/V, issued
+    asynchronously while the rank's own chunk pairs are computed, then the
+    remaining pairs. On 8 B200s NCCL point-to-point between ring neighbours ran
+    at about 80 GB/s per GPU while the all-gather moves the same bytes at
+    collective bandwidth, so "allgather" is the faster schedule there.
     """
     import torch
     import torch.distributed as dist
 
     compute = compute or _default_compute(softmax_scale)
     merge = merge or _default_merge
+    if schedule == "allgather":
+        return _allgather_attention(q_loc, k_loc, v_loc_bhds, zz, rank, group, compute, merge)
+    if schedule != "ring":
+        raise ValueError(f"unknown schedule {schedule!r}")
     W, c = zz.world, zz.chunk
     my_chunks = zz.chunks_of(rank)
     q_parts = [q_loc.narrow(2, 0, c), q_loc.narrow(2, c, c)]
@@ -149,6 +162,59 @@ def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
         if step + 1 < W:
             cur_k, nxt_k = nxt_k, cur_k
             cur_v, nxt_v = nxt_v, cur_v
+    outs, lses = [], []
+    for qi in range(2):
+        o, l = merge(partial_o[qi], partial_l[qi])
+        outs.append(o)
+        lses.append(l)
+    return torch.cat(outs, dim=2), torch.cat(lses, dim=2)
+
+
+def _allgather_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group, compute, merge):
+    import torch
+    import torch.distributed as dist
+
+    W, c = zz.world, zz.chunk
+    my_chunks = zz.chunks_of(rank)
+    q_parts = [q_loc.narrow(2, 0, c), q_loc.narrow(2, c, c)]
+    k_loc, v_loc = k_loc.contiguous(), v_loc_bhds.contiguous()
+    k_all = torch.empty((W,) + tuple(k_loc.shape), dtype=k_loc.dtype, device=k_loc.device)
+    v_all = torch.empty((W,) + tuple(v_loc.shape), dtype=v_loc.dtype, device=v_loc.device)
+    works = []
+    if W > 1:
+        u8 = lambda t: t.view(torch.uint8)  # noqa: E731  (e4m3 travels as raw bytes)
+        if dist.get_backend(group) == "nccl":
+            works.append(dist.all_gather_into_tensor(u8(k_all), u8(k_loc), group=group,
+                                                     async_op=True))
+            works.append(dist.all_gather_into_tensor(u8(v_all), u8(v_loc), group=group,
+                                                     async_op=True))
+        else:  # gloo (CPU ranks): list form
+            works.append(dist.all_gather(list(u8(k_all).unbind(0)), u8(k_loc), group=group,
+                                         async_op=True))
+            works.append(dist.all_gather(list(u8(v_all).unbind(0)), u8(v_loc), group=group,
+                                         async_op=True))
+    else:
+        k_all[0].copy_(k_loc)
+        v_all[0].copy_(v_loc)
+    partial_o: List[list] = [[], []]
+    partial_l: List[list] = [[], []]
+
+    def run_pairs(src, k_src, v_src):
+        for qi, qc in enumerate(my_chunks):
+            for kj, kc in enumerate(zz.chunks_of(src)):
+                if not zz.visible(qc, kc):
+                    continue
+                o, l = compute(q_parts[qi], k_src.narrow(2, kj * c, c),
+                               v_src.narrow(3, kj * c, c), zz.start(qc), zz.start(kc))
+                partial_o[qi].append(o)
+                partial_l[qi].append(l)
+
+    run_pairs(rank, k_loc, v_loc)          # own chunks while the gather runs
+    for w in works:
+        w.wait()
+    for step in range(1, W):
+        src = zz.source_rank(rank, step)
+        run_pairs(src, k_all[src], v_all[src])
     outs, lses = [], []
     for qi in range(2):
         o, l = merge(partial_o[qi], partial_l[qi])

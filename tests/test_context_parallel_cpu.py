@@ -46,7 +46,7 @@ def cpu_merge(outs, lses):
     return o, lse
 
 
-def _worker(rank, world, port, S, out_q):
+def _worker(rank, world, port, S, out_q, schedule="ring"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     B, H, D = 1, 2, 64
@@ -56,7 +56,7 @@ def _worker(rank, world, port, S, out_q):
     zz = cp.ZigZag(world, S)
     o_loc, l_loc = cp.ring_attention(cp.split_local(q, zz, rank, 2), cp.split_local(k, zz, rank, 2),
                                      cp.split_local(v, zz, rank, 3), zz, rank,
-                                     compute=cpu_compute, merge=cpu_merge)
+                                     compute=cpu_compute, merge=cpu_merge, schedule=schedule)
     o = cp.gather_full(o_loc, zz, dim=2)
     l = cp.gather_full(l_loc.unsqueeze(-1), zz, dim=2).squeeze(-1)
     if rank == 0:
@@ -65,13 +65,15 @@ def _worker(rank, world, port, S, out_q):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ring_matches_single_device_oracle(world):
+@pytest.mark.parametrize("world,schedule", [(2, "ring"), (4, "ring"), (2, "allgather"),
+                                            (4, "allgather")])
+def test_ring_matches_single_device_oracle(world, schedule):
     S = 64 * 2 * world
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, S, q_out)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, S, q_out, schedule))
+             for r in range(world)]
     for p in procs:
         p.start()
     o, l = q_out.get(timeout=300)
