@@ -262,6 +262,12 @@ extern "C" int fa8_trace_cta_fetch(long long* host_buf) {
              ? 0
              : 1;
 }
+extern "C" int fa8_trace_spin_fetch(unsigned long long* host_buf) {
+  return cudaMemcpyFromSymbol(host_buf, fa8::fa8_trace_spin, sizeof(fa8::fa8_trace_spin)) ==
+                 cudaSuccess
+             ? 0
+             : 1;
+}
 extern "C" int fa8_trace_fetch(long long* host_buf) {
   return cudaMemcpyFromSymbol(host_buf, fa8::fa8_trace_buf, sizeof(fa8::fa8_trace_buf)) ==
                  cudaSuccess

@@ -141,6 +141,8 @@ struct KernelParams {
 // Debug-only phase timestamps (clock64) of CTA (0,0,0): [role][step][event].
 // role 0/1 = softmax warpgroup 0/1 (thread 0 of the group), role 2 = MMA thread.
 __device__ long long fa8_trace_buf[3][64][8];
+// [slot]: waits that did not succeed on the first probe; [64 + slot]: polls.
+__device__ unsigned long long fa8_trace_spin[128];
 // Per-CTA (linear block id < 4096): globaltimer at entry and exit, SM id.
 __device__ long long fa8_trace_cta[4096][3];
 __device__ __forceinline__ long long fa8_gtimer() {
@@ -178,7 +180,19 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
                                              volatile int* abort_flag, int* status) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
+#ifdef FA8_TRACE
+  // Debug: count polls per barrier slot (CTA 0 only).
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+    extern __shared__ uint8_t smem_raw[];
+    (void)smem_raw;
+    atomicAdd(&fa8_trace_spin[(ptx::smem_u32(bar) & 0x3ff) / 8], 1ull);
+  }
+#endif
   while (true) {
+#ifdef FA8_TRACE
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+      atomicAdd(&fa8_trace_spin[64 + (ptx::smem_u32(bar) & 0x3ff) / 8], 1ull);
+#endif
 #if FA8_WAIT_SLEEP
     // Suspends until the phase completes (or the hint expires): a waiting warp
     // takes no issue slots from the warps that share its scheduler.
