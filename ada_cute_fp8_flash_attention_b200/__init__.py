@@ -57,7 +57,8 @@ def flash_attn_fp8_forward(q, k, v):
 
 def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout="bhds",
                               return_lse=False, out_dtype="fp16", q_offset=0, kv_offset=0,
-                              split_keys=-1, out=None, lse=None):
+                              split_keys=-1, out=None, lse=None, descale_q=1.0, descale_k=1.0,
+                              descale_v=1.0):
     """FP8 attention forward with options.
 
     Returns ``out`` or ``(out, lse)`` when ``return_lse`` is set. ``lse`` is the
@@ -65,10 +66,12 @@ def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout
     ``-inf`` for rows with no visible key. ``q_offset``/``kv_offset`` are global
     positions used by the causal mask (context-parallel chunks). ``split_keys``:
     query tiles whose first row sees fewer keys than this use a two-term (hi +
-    lo) e4m3 P; -1 = default (1024), 0 = never.
+    lo) e4m3 P; -1 = default (1024), 0 = never. ``descale_q/k/v``: per-tensor
+    dequantisation factors of scaled e4m3 inputs (real value = code x factor).
     """
     res = _C.flash_attn_fp8_forward_ex(q, k, v, causal, softmax_scale, v_layout, return_lse,
-                                       out_dtype, q_offset, kv_offset, split_keys, out, lse)
+                                       out_dtype, q_offset, kv_offset, split_keys, out, lse,
+                                       descale_q, descale_k, descale_v)
     return (res[0], res[1]) if return_lse else res[0]
 
 

@@ -50,6 +50,8 @@ class Fa8FwdParams(C.Structure):
         ("out_dtype", C.c_int32),
         ("q_offset", C.c_int64), ("kv_offset", C.c_int64),
         ("split_keys", C.c_int32), ("max_ctas", C.c_int32),
+        ("descale_q", C.c_float), ("descale_k", C.c_float), ("descale_v", C.c_float),
+        ("reserved0", C.c_int32),
     ]
 
 

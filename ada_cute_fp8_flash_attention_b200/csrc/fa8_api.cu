@@ -124,7 +124,8 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.split_keys = p->split_keys < 0 ? fa8::kDefaultSplitKeys : p->split_keys;
   const int rows_per_cta = T * fa8::kBlockM;
   kp.n_qblocks = (int)((p->seqlen_q + rows_per_cta - 1) / rows_per_cta);
-  kp.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  kp.scale_log2 = p->softmax_scale * p->descale_q * p->descale_k * 1.4426950408889634f;
+  kp.o_scale = p->descale_v;
   kp.q_offset = p->q_offset;
   kp.kv_offset = p->kv_offset;
   kp.o = p->o;
@@ -176,6 +177,9 @@ void fa8_fwd_params_init(fa8_fwd_params* p, int64_t batch, int64_t heads, int64_
   p->v_layout = FA8_V_BHDS;
   p->out_dtype = FA8_OUT_F16;
   p->split_keys = -1;
+  p->descale_q = 1.0f;
+  p->descale_k = 1.0f;
+  p->descale_v = 1.0f;
 }
 
 int fa8_fwd(const fa8_fwd_params* p, void* stream) {
@@ -198,6 +202,9 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
     return set_msg(FA8_ERR_INVALID_ARG, "null tensor pointer");
   if (!(p->softmax_scale > 0.f) || !std::isfinite(p->softmax_scale))
     return set_msg(FA8_ERR_INVALID_ARG, "softmax_scale must be positive and finite");
+  for (float d : {p->descale_q, p->descale_k, p->descale_v})
+    if (!(d > 0.f) || !std::isfinite(d))
+      return set_msg(FA8_ERR_INVALID_ARG, "descale factors must be positive and finite");
   if (!aligned16(p->q) || !aligned16(p->o) ||
       (p->seqlen_kv > 0 && (!aligned16(p->k) || !aligned16(p->v))))
     return set_msg(FA8_ERR_ALIGNMENT, "tensor base addresses must be 16-byte aligned");

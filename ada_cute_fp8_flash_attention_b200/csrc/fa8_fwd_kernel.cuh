@@ -128,7 +128,8 @@ struct TileCfg {
 struct KernelParams {
   int batch, heads, heads_kv, seqlen_q, seqlen_kv, head_group;
   int causal, out_e4m3, split_keys, n_qblocks;
-  float scale_log2;
+  float scale_log2;  // softmax scale x descale_q x descale_k x log2(e)
+  float o_scale;     // descale_v
   long long q_offset, kv_offset;
   void* o;
   long long o_sb, o_sh, o_ss;
@@ -654,7 +655,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
     if (r == 0) FA8_TR(i, 63, 1);
     if (tp[i].q_start < p.seqlen_q) {
       ptx::tc_fence_after();
-      const float inv_l = (l_run > 0.f && ok) ? 1.f / l_run : 0.f;
+      const float inv_l = (l_run > 0.f && ok) ? p.o_scale / l_run : 0.f;
       char* row_ptr = o_head + (long long)row * p.o_ss * (p.out_e4m3 ? 1 : 2);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {

@@ -51,7 +51,9 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
                                         const std::string& out_dtype, int64_t q_offset,
                                         int64_t kv_offset, int64_t split_keys,
                                         c10::optional<torch::Tensor> out_opt,
-                                        c10::optional<torch::Tensor> lse_opt) {
+                                        c10::optional<torch::Tensor> lse_opt,
+                                        double descale_q = 1.0, double descale_k = 1.0,
+                                        double descale_v = 1.0) {
   check_fp8_input(q, "q");
   check_fp8_input(k, "k");
   check_fp8_input(v, "v");
@@ -145,6 +147,9 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
   p.q_offset = q_offset;
   p.kv_offset = kv_offset;
   p.split_keys = static_cast<int32_t>(split_keys);
+  p.descale_q = static_cast<float>(descale_q);
+  p.descale_k = static_cast<float>(descale_k);
+  p.descale_v = static_cast<float>(descale_v);
   check_status(fa8_fwd(&p, stream.stream()), "fa8_fwd");
   if (lse.defined()) return {out, lse};
   return {out};
@@ -163,13 +168,14 @@ std::vector<torch::Tensor> flash_attn_fp8_forward_ex(
     torch::Tensor q, torch::Tensor k, torch::Tensor v, bool causal,
     c10::optional<double> softmax_scale, std::string v_layout, bool return_lse,
     std::string out_dtype, int64_t q_offset, int64_t kv_offset, int64_t split_keys,
-    c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> lse) {
+    c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> lse, double descale_q,
+    double descale_k, double descale_v) {
   TORCH_CHECK(q.dim() == 4, "q must be (B, H, S, D)");
   const double scale = softmax_scale.has_value()
                            ? *softmax_scale
                            : 1.0 / std::sqrt(static_cast<double>(q.size(3)));
   return forward_impl(q, k, v, causal, scale, v_layout, return_lse, out_dtype, q_offset,
-                      kv_offset, split_keys, out, lse);
+                      kv_offset, split_keys, out, lse, descale_q, descale_k, descale_v);
 }
 
 std::vector<torch::Tensor> lse_merge(std::vector<torch::Tensor> outs,
@@ -233,6 +239,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_layout") = "bhds", py::arg("return_lse") = false,
         py::arg("out_dtype") = "fp16", py::arg("q_offset") = 0, py::arg("kv_offset") = 0,
         py::arg("split_keys") = -1, py::arg("out") = py::none(), py::arg("lse") = py::none(),
+        py::arg("descale_q") = 1.0, py::arg("descale_k") = 1.0, py::arg("descale_v") = 1.0,
         "FP8 attention forward with options; returns [out] or [out, lse]");
   m.def("lse_merge", &lse_merge, "log-sum-exp merge of partial attention outputs");
   m.def("quantize_e4m3", &quantize_e4m3, py::arg("x"), py::arg("scale") = 1.0,

@@ -92,10 +92,19 @@ typedef struct fa8_fwd_params {
   int32_t split_keys;
   /* Upper bound on resident CTAs (0 = all SMs). */
   int32_t max_ctas;
+
+  /* Per-tensor dequantisation factors of e4m3 Q, K, V (real value = code x
+   * factor); 1.0 = unscaled inputs. The kernel folds descale_q * descale_k
+   * into the softmax scale and multiplies O by descale_v. */
+  float descale_q;
+  float descale_k;
+  float descale_v;
+  int32_t reserved0;
 } fa8_fwd_params;
 
 /* Fill *p with defaults: contiguous strides for the given shape, scale
- * 1/sqrt(head_dim), non-causal, BHDS V, fp16 out, default split. */
+ * 1/sqrt(head_dim), non-causal, BHDS V, fp16 out, default split, unit
+ * dequantisation factors. */
 void fa8_fwd_params_init(fa8_fwd_params* p, int64_t batch, int64_t heads,
                          int64_t heads_kv, int64_t seqlen_q, int64_t seqlen_kv,
                          int64_t head_dim);

@@ -153,3 +153,17 @@ def test_empty_and_zero_kv(fa8, cuda):
     q0 = torch.empty((1, 2, 0, 64), dtype=torch.float8_e4m3fn, device=cuda)
     out0 = fa8.flash_attn_fp8_forward_ex(q0, q0, vd, causal=True)
     assert out0.shape == (1, 2, 0, 64)
+
+
+def test_per_tensor_descale(fa8, cuda):
+    """Scaled e4m3 inputs (real = code x factor): scores use dq*dk, O uses dv."""
+    q, k, v = U.inputs(1, 2, 2, 256, 384, 128, "normal", 1.0, seed=21)
+    dq, dk, dv = 0.37, 0.6, 2.5
+    out, lse = run_ex(fa8, q, k, v, cuda, causal=True, return_lse=True, descale_q=dq,
+                      descale_k=dk, descale_v=dv)
+    from oracle import attention_ref as ref
+    o_ref, l_ref = ref.attention(ref.e4m3_decode(q) * dq, ref.e4m3_decode(k) * dk,
+                                 ref.e4m3_decode(v) * dv, True)
+    U.assert_close(out.float().cpu().numpy(), o_ref, max_abs=U.MAX_ABS * dv,
+                   mean_abs=U.MEAN_ABS * dv)
+    assert np.abs(lse.cpu().numpy() - l_ref).max() < 1e-3
