@@ -25,6 +25,7 @@ from . import _build
 __all__ = [
     "flash_attn_fp8_forward",
     "flash_attn_fp8_forward_ex",
+    "flash_attn_fp8_varlen_forward",
     "lse_merge",
     "quantize_e4m3",
     "launch_count",
@@ -72,6 +73,23 @@ def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout
     res = _C.flash_attn_fp8_forward_ex(q, k, v, causal, softmax_scale, v_layout, return_lse,
                                        out_dtype, q_offset, kv_offset, split_keys, out, lse,
                                        descale_q, descale_k, descale_v)
+    return (res[0], res[1]) if return_lse else res[0]
+
+
+def flash_attn_fp8_varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_kv, max_seqlen_q,
+                                  causal=True, softmax_scale=None, v_layout="thd",
+                                  return_lse=False, out_dtype="fp16"):
+    """FP8 attention over packed variable-length sequences.
+
+    q: (total_q, H, D), k: (total_kv, H_kv, D), v: (total_kv, H_kv, D) ("thd") or
+    (H_kv, D, total_kv) ("hdt"), all e4m3; cu_seqlens_*: int32 prefix sums (batch+1).
+    Every cu_seqlens_kv entry must be a multiple of 16. The cu_seqlens are read on
+    the host for validation (one device-to-host copy when they live on the GPU).
+    Returns out (total_q, H, D) or (out, lse (H, total_q)).
+    """
+    res = _C.flash_attn_fp8_varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_kv,
+                                           int(max_seqlen_q), causal, softmax_scale, v_layout,
+                                           return_lse, out_dtype)
     return (res[0], res[1]) if return_lse else res[0]
 
 

@@ -52,6 +52,8 @@ class Fa8FwdParams(C.Structure):
         ("split_keys", C.c_int32), ("max_ctas", C.c_int32),
         ("descale_q", C.c_float), ("descale_k", C.c_float), ("descale_v", C.c_float),
         ("reserved0", C.c_int32),
+        ("cu_seqlens_q", C.c_void_p), ("cu_seqlens_kv", C.c_void_p),
+        ("max_seqlen_q", C.c_int64),
     ]
 
 

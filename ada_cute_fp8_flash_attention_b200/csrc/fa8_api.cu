@@ -101,15 +101,23 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   CUtensorMap tq, tk, tv;
   memset(&tk, 0, sizeof(tk));
   memset(&tv, 0, sizeof(tv));
-  st = make_map_u8(&tq, p->q, D, p->seqlen_q, p->heads, p->batch, p->q_stride_s, p->q_stride_h,
-                   p->q_stride_b, D, fa8::kBlockM, swz_qk);
+  // Packed variable-length layout: one "batch" of total rows per map.
+  const bool varlen = p->cu_seqlens_q != nullptr;
+  const uint64_t nb = varlen ? 1 : (uint64_t)p->batch;
+  const uint64_t qsb = varlen ? 16 : (uint64_t)p->q_stride_b;
+  const uint64_t ksb = varlen ? 16 : (uint64_t)p->k_stride_b;
+  const uint64_t vsb = varlen ? 16 : (uint64_t)p->v_stride_b;
+  st = make_map_u8(&tq, p->q, D, p->seqlen_q, p->heads, nb, p->q_stride_s, p->q_stride_h, qsb, D,
+                   fa8::kBlockM, swz_qk);
   if (st) return st;
-  if (p->seqlen_kv > 0) st = make_map_u8(&tk, p->k, D, p->seqlen_kv, p->heads_kv, p->batch, p->k_stride_s,
-                   p->k_stride_h, p->k_stride_b, D, fa8::kBlockN, swz_qk);
+  if (p->seqlen_kv > 0)
+    st = make_map_u8(&tk, p->k, D, p->seqlen_kv, p->heads_kv, nb, p->k_stride_s, p->k_stride_h,
+                     ksb, D, fa8::kBlockN, swz_qk);
   if (st) return st;
   // V^T (BHDS): innermost = keys, rows = d.
-  if (p->seqlen_kv > 0) st = make_map_u8(&tv, p->v, p->seqlen_kv, D, p->heads_kv, p->batch, p->v_stride_r,
-                   p->v_stride_h, p->v_stride_b, fa8::kBlockN, D, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (p->seqlen_kv > 0)
+    st = make_map_u8(&tv, p->v, p->seqlen_kv, D, p->heads_kv, nb, p->v_stride_r, p->v_stride_h,
+                     vsb, fa8::kBlockN, D, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
 
   fa8::KernelParams kp;
@@ -123,7 +131,10 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.out_e4m3 = p->out_dtype == FA8_OUT_E4M3 ? 1 : 0;
   kp.split_keys = p->split_keys < 0 ? fa8::kDefaultSplitKeys : p->split_keys;
   const int rows_per_cta = T * fa8::kBlockM;
-  kp.n_qblocks = (int)((p->seqlen_q + rows_per_cta - 1) / rows_per_cta);
+  const int64_t rows = varlen ? p->max_seqlen_q : p->seqlen_q;
+  kp.n_qblocks = (int)((rows + rows_per_cta - 1) / rows_per_cta);
+  kp.cu_seqlens_q = p->cu_seqlens_q;
+  kp.cu_seqlens_kv = p->cu_seqlens_kv;
   kp.scale_log2 = p->softmax_scale * p->descale_q * p->descale_k * 1.4426950408889634f;
   kp.o_scale = p->descale_v;
   kp.q_offset = p->q_offset;
@@ -136,6 +147,10 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.lse_sb = p->lse_stride_b;
   kp.lse_sh = p->lse_stride_h;
   kp.status = p->status;
+  if (varlen) {  // sequences are addressed by their packed row offsets
+    kp.o_sb = 0;
+    kp.lse_sb = 0;
+  }
 
   dim3 grid(kp.n_qblocks, (unsigned)p->heads, (unsigned)p->batch);
   fa8::fa8_fwd_kernel<D, T><<<grid, fa8::Roles<T>::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, kp);
@@ -193,6 +208,14 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
   if (p->out_dtype != FA8_OUT_F16 && p->out_dtype != FA8_OUT_E4M3)
     return set_msg(FA8_ERR_INVALID_ARG, "out_dtype must be FA8_OUT_F16 or FA8_OUT_E4M3");
   if (p->batch == 0 || p->heads == 0 || p->seqlen_q == 0) return FA8_OK;
+  if (p->cu_seqlens_q || p->cu_seqlens_kv) {
+    if (!p->cu_seqlens_q || !p->cu_seqlens_kv)
+      return set_msg(FA8_ERR_INVALID_ARG, "varlen needs both cu_seqlens_q and cu_seqlens_kv");
+    if (p->max_seqlen_q <= 0 || p->max_seqlen_q > p->seqlen_q)
+      return set_msg(FA8_ERR_INVALID_ARG, "varlen needs 0 < max_seqlen_q <= total query rows");
+    if (p->q_offset || p->kv_offset)
+      return set_msg(FA8_ERR_UNSUPPORTED, "varlen does not take context-parallel offsets");
+  }
   if (p->heads_kv <= 0 || p->heads % p->heads_kv != 0)
     return set_msg(FA8_ERR_UNSUPPORTED, "heads must be a multiple of heads_kv");
   if (p->batch > 65535 || p->heads > 65535 || p->seqlen_q > (1ll << 30) ||

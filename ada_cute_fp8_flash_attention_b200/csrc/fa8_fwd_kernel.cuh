@@ -136,6 +136,8 @@ struct KernelParams {
   float* lse;
   long long lse_sb, lse_sh;
   int* status;
+  const int* cu_seqlens_q;   // varlen: (batch + 1) prefix sums, or null
+  const int* cu_seqlens_kv;
 };
 
 #ifdef FA8_TRACE
@@ -220,23 +222,24 @@ struct TilePlan {
 };
 
 template <int kTilesPerCta>
-__device__ __forceinline__ TilePlan plan_tile(const KernelParams& p, int qb, int i) {
+__device__ __forceinline__ TilePlan plan_tile(const KernelParams& p, int qb, int i, int sq,
+                                              int skv) {
   TilePlan t;
   t.q_start = qb * (kTilesPerCta * kBlockM) + i * kBlockM;
   t.n = 0;
   t.split = 0;
-  if (t.q_start >= p.seqlen_q) return t;
-  const int n_kv = (p.seqlen_kv + kBlockN - 1) / kBlockN;
+  if (t.q_start >= sq) return t;
+  const int n_kv = (skv + kBlockN - 1) / kBlockN;
   long long visible_first;
   if (p.causal) {
-    const long long last_row = min(t.q_start + kBlockM - 1, p.seqlen_q - 1);
+    const long long last_row = min(t.q_start + kBlockM - 1, sq - 1);
     const long long max_key = p.q_offset + last_row - p.kv_offset;  // local key index
     t.n = max_key < 0 ? 0 : (int)min((long long)n_kv, max_key / kBlockN + 1);
     visible_first = p.q_offset + t.q_start - p.kv_offset + 1;
-    if (visible_first > p.seqlen_kv) visible_first = p.seqlen_kv;
+    if (visible_first > skv) visible_first = skv;
   } else {
     t.n = n_kv;
-    visible_first = p.seqlen_kv;
+    visible_first = skv;
   }
   t.split = (t.n > 0 && visible_first < p.split_keys) ? 1 : 0;
   return t;
@@ -306,24 +309,41 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int hk = h / p.head_group;
+  // Variable-length batches: sequence b occupies rows [cu[b], cu[b+1]) of the
+  // packed Q / O (and K / V^T) tensors; the TMA batch coordinate is then 0.
+  int sq = p.seqlen_q, skv = p.seqlen_kv, q_base = 0, kv_base = 0, tb = b;
+  if (p.cu_seqlens_q) {
+    q_base = p.cu_seqlens_q[b];
+    sq = p.cu_seqlens_q[b + 1] - q_base;
+    kv_base = p.cu_seqlens_kv[b];
+    skv = p.cu_seqlens_kv[b + 1] - kv_base;
+    tb = 0;
+    if ((kv_base & 15) != 0 || sq < 0 || skv < 0) {
+      // A V^T tile must start on a 16-byte boundary (TMA): refuse the sequence.
+      if (threadIdx.x == 0 && p.status) atomicOr(p.status, 2);
+      return;
+    }
+  }
 
   TilePlan tp[kTilesPerCta];
 #pragma unroll
-  for (int i = 0; i < kTilesPerCta; ++i) tp[i] = plan_tile<kTilesPerCta>(p, qb, i);
+  for (int i = 0; i < kTilesPerCta; ++i) tp[i] = plan_tile<kTilesPerCta>(p, qb, i, sq, skv);
   int nmax = 0;
 #pragma unroll
   for (int i = 0; i < kTilesPerCta; ++i) nmax = max(nmax, tp[i].n);
 
   char* o_head = reinterpret_cast<char*>(p.o) +
-                 ((long long)b * p.o_sb + (long long)h * p.o_sh) * (p.out_e4m3 ? 1 : 2);
-  float* lse_head = p.lse ? p.lse + (long long)b * p.lse_sb + (long long)h * p.lse_sh : nullptr;
+                 ((long long)b * p.o_sb + (long long)h * p.o_sh + (long long)q_base * p.o_ss) *
+                     (p.out_e4m3 ? 1 : 2);
+  float* lse_head =
+      p.lse ? p.lse + (long long)b * p.lse_sb + (long long)h * p.lse_sh + q_base : nullptr;
 
   if (nmax == 0) {
     // Every row of this CTA is fully masked: O = 0, LSE = -inf.
     if (warp < kSoftmaxWarps) {
       const int i = warp / 4;
       const int row = tp[i].q_start + (threadIdx.x % kBlockM);
-      if (tp[i].q_start < p.seqlen_q && row < p.seqlen_q) {
+      if (tp[i].q_start < sq && row < sq) {
         float z[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) z[j] = 0.f;
@@ -395,7 +415,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         if (tp[i].n == 0) continue;
         ptx::mbar_arrive_expect_tx(&bars.q_full[i], C::kQBytes);
         ptx::tma_load_4d(smem + C::kOffQ + i * C::kQBytes, &tm_q, &bars.q_full[i], 0,
-                         tp[i].q_start, h, b, pol_q);
+                         q_base + tp[i].q_start, h, tb, pol_q);
       }
       int issued = 0;
       bool ok = true;
@@ -409,9 +429,11 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
           ptx::mbar_arrive_expect_tx(&bars.kv_full[st], C::kStageBytes);
           uint8_t* dst = smem + C::kOffRing + st * C::kStageBytes;
           if (part == 0)
-            ptx::tma_load_4d(dst, &tm_k, &bars.kv_full[st], 0, kv * kBlockN, hk, b, pol_kv);
+            ptx::tma_load_4d(dst, &tm_k, &bars.kv_full[st], 0, kv_base + kv * kBlockN, hk, tb,
+                             pol_kv);
           else
-            ptx::tma_load_4d(dst, &tm_v, &bars.kv_full[st], kv * kBlockN, 0, hk, b, pol_kv);
+            ptx::tma_load_4d(dst, &tm_v, &bars.kv_full[st], kv_base + kv * kBlockN, 0, hk, tb,
+                             pol_kv);
           ++issued;
         }
       }
@@ -570,7 +592,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       // seqlen_kv, or, causal, keys after the tile's first query)
       const int kv0 = kv * kBlockN;
       const bool tile_masked =
-          (kv0 + kBlockN > p.seqlen_kv) ||
+          (kv0 + kBlockN > skv) ||
           (p.causal && p.kv_offset + kv0 + kBlockN - 1 > p.q_offset + tp[i].q_start);
       uint32_t ph[kBlockN / 4];
       uint32_t pl[kBlockN / 4];
@@ -587,7 +609,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, false, m_run, l_run, ph, pl);
       } else {
         // Mask: keys past seqlen_kv, and (causal) keys after this query.
-        long long lim = p.seqlen_kv - kv0;
+        long long lim = skv - kv0;
         if (p.causal) lim = min(lim, row_g - p.kv_offset - kv0 + 1);
         if (lim < kBlockN) {
           const int li = (int)max(lim, -1LL);
@@ -653,7 +675,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
     if (r == 0) FA8_TR(i, 63, 0);
     if (n > 0 && ok) ok = bounded_wait(&bars.o_done[i], (n - 1) & 1, abort_flag, p.status);
     if (r == 0) FA8_TR(i, 63, 1);
-    if (tp[i].q_start < p.seqlen_q) {
+    if (tp[i].q_start < sq) {
       ptx::tc_fence_after();
       const float inv_l = (l_run > 0.f && ok) ? p.o_scale / l_run : 0.f;
       char* row_ptr = o_head + (long long)row * p.o_ss * (p.out_e4m3 ? 1 : 2);
@@ -671,9 +693,9 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
-        if (row < p.seqlen_q) store_o_chunk(p, row_ptr, c, v);
+        if (row < sq) store_o_chunk(p, row_ptr, c, v);
       }
-      if (lse_head && row < p.seqlen_q) {
+      if (lse_head && row < sq) {
         const float base = m_run - kPShift;
         lse_head[row] =
             (l_run > 0.f) ? (__log2f(l_run) + base) * 0.69314718055994531f : -INFINITY;

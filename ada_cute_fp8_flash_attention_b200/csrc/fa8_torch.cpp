@@ -178,6 +178,85 @@ std::vector<torch::Tensor> flash_attn_fp8_forward_ex(
                       kv_offset, split_keys, out, lse, descale_q, descale_k, descale_v);
 }
 
+// Variable-length (packed) batches: q (total_q, H, D), k (total_kv, H_kv, D),
+// v (total_kv, H_kv, D) ("thd") or pre-transposed (H_kv, D, total_kv) ("hdt");
+// cu_seqlens_* int32 (batch + 1). Returns [out (total_q, H, D)] (+ lse (H, total_q)).
+std::vector<torch::Tensor> flash_attn_fp8_varlen_forward(
+    torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens_q,
+    torch::Tensor cu_seqlens_kv, int64_t max_seqlen_q, bool causal,
+    c10::optional<double> softmax_scale, std::string v_layout, bool return_lse,
+    std::string out_dtype) {
+  for (auto* t : {&q, &k, &v}) {
+    TORCH_CHECK(t->device().is_cuda() && t->scalar_type() == at::ScalarType::Float8_e4m3fn,
+                "q, k, v must be CUDA float8_e4m3fn tensors");
+    TORCH_CHECK(t->dim() == 3, "q, k, v must be 3-D (packed)");
+  }
+  TORCH_CHECK(v_layout == "thd" || v_layout == "hdt", "v_layout must be 'thd' or 'hdt'");
+  TORCH_CHECK(out_dtype == "fp16" || out_dtype == "e4m3", "out_dtype must be 'fp16' or 'e4m3'");
+  const int64_t Tq = q.size(0), H = q.size(1), D = q.size(2);
+  const int64_t Tk = k.size(0), Hkv = k.size(1);
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
+  TORCH_CHECK(k.size(2) == D && Hkv > 0 && H % Hkv == 0, "k must be (total_kv, H_kv, D)");
+  TORCH_CHECK(cu_seqlens_q.dim() == 1 && cu_seqlens_q.numel() >= 2 &&
+                  cu_seqlens_kv.numel() == cu_seqlens_q.numel(),
+              "cu_seqlens_q / cu_seqlens_kv must be 1-D with batch + 1 entries");
+  const int64_t B = cu_seqlens_q.numel() - 1;
+  auto cuq_h = cu_seqlens_q.to(at::kCPU).to(at::kInt);
+  auto cuk_h = cu_seqlens_kv.to(at::kCPU).to(at::kInt);
+  const int* cq = cuq_h.data_ptr<int>();
+  const int* ck = cuk_h.data_ptr<int>();
+  TORCH_CHECK(cq[0] == 0 && ck[0] == 0 && cq[B] == Tq && ck[B] == Tk,
+              "cu_seqlens must start at 0 and end at the packed lengths");
+  for (int64_t b = 0; b < B; ++b) {
+    TORCH_CHECK(cq[b + 1] >= cq[b] && ck[b + 1] >= ck[b], "cu_seqlens must be non-decreasing");
+    TORCH_CHECK(cq[b + 1] - cq[b] <= max_seqlen_q, "a sequence is longer than max_seqlen_q");
+    TORCH_CHECK(ck[b] % 16 == 0,
+                "every cu_seqlens_kv entry must be a multiple of 16 (V^T tile alignment)");
+  }
+  c10::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream(q.get_device());
+  q = q.contiguous();
+  k = k.contiguous();
+  const int64_t Tk_pad = (Tk + 15) / 16 * 16;
+  torch::Tensor vt = torch::zeros({Hkv, D, Tk_pad}, v.options());
+  if (v_layout == "thd") {
+    TORCH_CHECK(v.size(0) == Tk && v.size(1) == Hkv && v.size(2) == D, "v must be (total_kv, H_kv, D)");
+    vt.narrow(2, 0, Tk).copy_(v.permute({1, 2, 0}));
+  } else {
+    TORCH_CHECK(v.size(0) == Hkv && v.size(1) == D && v.size(2) == Tk, "v must be (H_kv, D, total_kv)");
+    vt.narrow(2, 0, Tk).copy_(v);
+  }
+  const bool e4m3_out = out_dtype == "e4m3";
+  auto out = torch::empty({Tq, H, D}, q.options().dtype(e4m3_out ? at::ScalarType::Float8_e4m3fn
+                                                                    : at::ScalarType::Half));
+  torch::Tensor lse;
+  if (return_lse) lse = torch::empty({H, Tq}, q.options().dtype(at::ScalarType::Float));
+  auto cuq_d = cuq_h.to(q.device());
+  auto cuk_d = cuk_h.to(q.device());
+  fa8_fwd_params p;
+  fa8_fwd_params_init(&p, B, H, Hkv, Tq, Tk, D);
+  p.q = q.data_ptr();
+  p.k = k.data_ptr();
+  p.v = vt.data_ptr();
+  p.o = out.data_ptr();
+  p.lse = return_lse ? lse.data_ptr<float>() : nullptr;
+  p.q_stride_s = H * D;  p.q_stride_h = D;  p.q_stride_b = Tq * H * D;
+  p.k_stride_s = Hkv * D; p.k_stride_h = D; p.k_stride_b = Tk * Hkv * D;
+  p.v_stride_r = Tk_pad; p.v_stride_h = D * Tk_pad; p.v_stride_b = Hkv * D * Tk_pad;
+  p.o_stride_s = H * D;  p.o_stride_h = D;  p.o_stride_b = 0;
+  p.lse_stride_h = Tq;   p.lse_stride_b = 0;
+  p.softmax_scale = static_cast<float>(softmax_scale.has_value() ? *softmax_scale
+                                                                 : 1.0 / std::sqrt((double)D));
+  p.causal = causal ? 1 : 0;
+  p.out_dtype = e4m3_out ? FA8_OUT_E4M3 : FA8_OUT_F16;
+  p.cu_seqlens_q = cuq_d.data_ptr<int>();
+  p.cu_seqlens_kv = cuk_d.data_ptr<int>();
+  p.max_seqlen_q = max_seqlen_q;
+  check_status(fa8_fwd(&p, stream.stream()), "fa8_fwd (varlen)");
+  if (return_lse) return {out, lse};
+  return {out};
+}
+
 std::vector<torch::Tensor> lse_merge(std::vector<torch::Tensor> outs,
                                      std::vector<torch::Tensor> lses) {
   TORCH_CHECK(!outs.empty() && outs.size() == lses.size() && outs.size() <= 16,
@@ -241,6 +320,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("split_keys") = -1, py::arg("out") = py::none(), py::arg("lse") = py::none(),
         py::arg("descale_q") = 1.0, py::arg("descale_k") = 1.0, py::arg("descale_v") = 1.0,
         "FP8 attention forward with options; returns [out] or [out, lse]");
+  m.def("flash_attn_fp8_varlen_forward", &flash_attn_fp8_varlen_forward, py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("cu_seqlens_q"), py::arg("cu_seqlens_kv"),
+        py::arg("max_seqlen_q"), py::arg("causal") = true, py::arg("softmax_scale") = py::none(),
+        py::arg("v_layout") = "thd", py::arg("return_lse") = false,
+        py::arg("out_dtype") = "fp16",
+        "FP8 attention over packed variable-length sequences; returns [out] or [out, lse]");
   m.def("lse_merge", &lse_merge, "log-sum-exp merge of partial attention outputs");
   m.def("quantize_e4m3", &quantize_e4m3, py::arg("x"), py::arg("scale") = 1.0,
         py::arg("transpose_last2") = false, "fp16/bf16 -> e4m3 (optionally transposed)");

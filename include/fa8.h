@@ -47,7 +47,7 @@ enum { FA8_V_BHDS = 0, FA8_V_BHSD = 1 };
 enum { FA8_OUT_F16 = 0, FA8_OUT_E4M3 = 1 };
 
 /* Bits the kernel ORs into *status when a bounded wait gives up. */
-enum { FA8_DEVERR_TIMEOUT = 1 };
+enum { FA8_DEVERR_TIMEOUT = 1, FA8_DEVERR_VARLEN_ALIGN = 2 };
 
 /*
  * All strides are in ELEMENTS. Tensors are indexed [b][h][s][d] for Q, K and
@@ -100,6 +100,19 @@ typedef struct fa8_fwd_params {
   float descale_k;
   float descale_v;
   int32_t reserved0;
+
+  /* Variable-length batches (optional). When cu_seqlens_q is non-NULL, Q/O
+   * and K/V hold `batch` sequences packed along the sequence dimension: Q is
+   * [total_q][heads][head_dim] (seqlen_q = total_q, q_stride_s = heads * D,
+   * q_stride_h = D), K likewise, V^T is [heads_kv][D][total_kv]; sequence b
+   * occupies rows cu_seqlens_q[b] .. cu_seqlens_q[b+1]-1 (device int32
+   * prefix sums with batch + 1 entries, same for cu_seqlens_kv). LSE is
+   * [heads][total_q]. Every cu_seqlens_kv[b] must be a multiple of 16 (V^T
+   * tiles start on 16-byte boundaries); a sequence that violates it is left
+   * unwritten and bit 2 is ORed into *status. max_seqlen_q bounds the grid. */
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_kv;
+  int64_t max_seqlen_q;
 } fa8_fwd_params;
 
 /* Fill *p with defaults: contiguous strides for the given shape, scale

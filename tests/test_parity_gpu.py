@@ -167,3 +167,46 @@ def test_per_tensor_descale(fa8, cuda):
     U.assert_close(out.float().cpu().numpy(), o_ref, max_abs=U.MAX_ABS * dv,
                    mean_abs=U.MEAN_ABS * dv)
     assert np.abs(lse.cpu().numpy() - l_ref).max() < 1e-3
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("D", [64, 128])
+def test_varlen_packed_sequences(fa8, cuda, causal, D):
+    """Packed batch of ragged sequences == each sequence run on its own."""
+    import torch
+    from oracle import attention_ref as ref
+    lens_q = [100, 257, 64, 1]
+    lens_k = [112, 256, 64, 16] if not causal else [112, 272, 64, 16]
+    if causal:
+        lens_q = [min(a, b) for a, b in zip(lens_q, lens_k)]
+    H, Hkv = 4, 2
+    cq = np.concatenate([[0], np.cumsum(lens_q)]).astype(np.int32)
+    ck = np.concatenate([[0], np.cumsum(lens_k)]).astype(np.int32)
+    q = ref.make_inputs((int(cq[-1]), H, D), "normal", 1)
+    k = ref.make_inputs((int(ck[-1]), Hkv, D), "normal", 2)
+    v = ref.make_inputs((int(ck[-1]), Hkv, D), "normal", 3)
+    out, lse = fa8.flash_attn_fp8_varlen_forward(
+        U.to_dev(q, cuda), U.to_dev(k, cuda), U.to_dev(v, cuda),
+        torch.from_numpy(cq).to(cuda), torch.from_numpy(ck).to(cuda), max(lens_q),
+        causal=causal, return_lse=True)
+    torch.cuda.synchronize()
+    out = out.float().cpu().numpy()
+    lse = lse.cpu().numpy()
+    for b in range(len(lens_q)):
+        qs, ks = slice(cq[b], cq[b + 1]), slice(ck[b], ck[b + 1])
+        qb = np.transpose(ref.e4m3_decode(q[qs]), (1, 0, 2))[None]
+        kb = np.transpose(ref.e4m3_decode(k[ks]), (1, 0, 2))[None]
+        vb = np.transpose(ref.e4m3_decode(v[ks]), (1, 2, 0))[None]
+        o_ref, l_ref = ref.attention(qb, kb, vb, causal)
+        U.assert_close(np.transpose(out[qs], (1, 0, 2))[None], o_ref, what=f"seq {b}")
+        fin = np.isfinite(l_ref[0])
+        assert np.abs(lse[:, qs][fin] - l_ref[0][fin]).max() < 1e-3
+
+
+def test_varlen_rejects_unaligned_kv_starts(fa8, cuda):
+    import torch
+    q = torch.zeros((30, 2, 64), dtype=torch.float8_e4m3fn, device=cuda)
+    k = torch.zeros((30, 2, 64), dtype=torch.float8_e4m3fn, device=cuda)
+    cu = torch.tensor([0, 10, 30], dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="multiple of 16"):
+        fa8.flash_attn_fp8_varlen_forward(q, k, k, cu, cu, 20)
