@@ -76,8 +76,8 @@ struct Roles {
   // setmaxnreg budgets: control + softmax registers must fit the launch budget
   // (65536 / kMinBlocks per CTA), and per scheduler 2 softmax warps + 1
   // control warp (x kMinBlocks CTAs) must fit its 512 registers per lane.
-  static constexpr int kRegsControl = (T == 1) ? 56 : 104;
-  static constexpr int kRegsSoftmax = 200;
+  static constexpr int kRegsControl = (T == 1) ? 64 : 104;
+  static constexpr int kRegsSoftmax = (T == 1) ? 192 : 200;
   static_assert(128 * kRegsControl + 128 * T * kRegsSoftmax <=
                     (65536 / kMinBlocks / (128 * (T + 1))) / 8 * 8 * 128 * (T + 1),
                 "setmaxnreg split exceeds the launch register budget");
