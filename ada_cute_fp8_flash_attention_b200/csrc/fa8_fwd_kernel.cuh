@@ -83,11 +83,11 @@ struct Roles {
                 "setmaxnreg split exceeds the launch register budget");
 };
 #ifndef FA8_EMU
-#define FA8_EMU 0
+#define FA8_EMU 2
 #endif
 // Columns of every 8 whose exp2 runs on the FMA pipe instead of MUFU. Measured
-// on B200: 0 is fastest in this kernel (the emulation adds issue pressure and
-// spills at the 168-register budget).
+// on B200 (C2 shape, one tile per CTA): 0 -> 1292 TFLOPS, 1 or 2 -> 1339,
+// 3 -> 1256; a degree-2 polynomial was no faster than degree 3.
 constexpr int kEmuPer8 = FA8_EMU;
 #ifndef FA8_STAGGER
 #define FA8_STAGGER 1

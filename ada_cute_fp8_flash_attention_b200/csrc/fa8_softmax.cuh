@@ -27,12 +27,20 @@ namespace fa8 {
 constexpr float kPShift = 6.0f;            // log2 of the P scale-up
 constexpr float kRescaleThreshold = 2.0f;  // log2 units; kPShift + it <= log2(448)
 
+#ifndef FA8_EMU_DEG
+#define FA8_EMU_DEG 3
+#endif
 namespace emu {
 // 2^f on [-0.5, 0.5]: c0 + f (c1 + f (c2 + f c3)), max relative error 7.7e-5.
 constexpr float kC0 = 0.999928891658783f;
 constexpr float kC1 = 0.6932758092880249f;
 constexpr float kC2 = 0.24260424077510834f;
 constexpr float kC3 = 0.05509091913700104f;
+// Degree-2 alternative: d0 + f (d1 + f d2), max relative error 1.8e-3 (well
+// below e4m3's 2^-4 rounding step of P).
+constexpr float kD0 = 1.0005117654800415f;
+constexpr float kD1 = 0.7033979296684265f;
+constexpr float kD2 = 0.23784694075584412f;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + magic rounds x to an integer
 constexpr float kClampLo = -30.0f;     // 2^-30 is far below e4m3's smallest subnormal
 }  // namespace emu
@@ -45,9 +53,14 @@ __device__ __forceinline__ uint64_t exp2_emu_pair(float x0, float x1) {
   const uint64_t t = ptx::fadd2(x, ptx::pack2(emu::kMagic, emu::kMagic));
   const uint64_t n = ptx::fadd2(t, ptx::pack2(-emu::kMagic, -emu::kMagic));
   const uint64_t f = ptx::ffma2(n, ptx::pack2(-1.f, -1.f), x);
+#if FA8_EMU_DEG == 2
+  uint64_t p = ptx::ffma2(ptx::pack2(emu::kD2, emu::kD2), f, ptx::pack2(emu::kD1, emu::kD1));
+  p = ptx::ffma2(p, f, ptx::pack2(emu::kD0, emu::kD0));
+#else
   uint64_t p = ptx::ffma2(ptx::pack2(emu::kC3, emu::kC3), f, ptx::pack2(emu::kC2, emu::kC2));
   p = ptx::ffma2(p, f, ptx::pack2(emu::kC1, emu::kC1));
   p = ptx::ffma2(p, f, ptx::pack2(emu::kC0, emu::kC0));
+#endif
   // bits(t) = bits(magic) + n; (bits(t) << 23) == n << 23 modulo 2^32.
   uint32_t t0, t1, p0, p1;
   asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t));
