@@ -38,7 +38,7 @@
 //   * P is formed as 2^(s*scale*log2e - m + kPShift) so typical
 //     probabilities sit in e4m3's normal range, not in its subnormals;
 //     with the lazy-rescale threshold the largest P is 2^(kPShift +
-//     kRescaleThreshold) = 256 < 448 (e4m3 max).
+//     kRescaleThreshold) = 2^8.75 = 430 < 448 (e4m3 max).
 //   * for query tiles whose rows see few keys (short causal prefixes) P is
 //     split as hi = e4m3(P), lo = e4m3(P - hi) and both are multiplied by V,
 //     which brings the relative error of P from 2^-4 to about 2^-8.

@@ -25,7 +25,11 @@
 namespace fa8 {
 
 constexpr float kPShift = 6.0f;            // log2 of the P scale-up
-constexpr float kRescaleThreshold = 2.0f;  // log2 units; kPShift + it <= log2(448)
+#ifndef FA8_RESCALE_THRESHOLD
+#define FA8_RESCALE_THRESHOLD 2.75f  // largest P = 2^(6 + 2.75) = 430
+#endif
+constexpr float kRescaleThreshold = FA8_RESCALE_THRESHOLD;  // log2 units
+static_assert(kPShift + kRescaleThreshold <= 8.8f, "largest P must stay below e4m3's 448");
 
 #ifndef FA8_EMU_DEG
 #define FA8_EMU_DEG 3

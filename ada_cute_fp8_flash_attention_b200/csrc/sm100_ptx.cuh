@@ -241,15 +241,34 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float a, float b) {
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
   return r;
 }
-// Four floats -> four e4m3 bytes in one word (a in the lowest byte).
+#ifndef FA8_CVT_RS
+#define FA8_CVT_RS 0
+#endif
+// Four floats -> four e4m3 bytes in one word (a in the lowest byte), RNE,
+// saturating.
+//
+// With FA8_CVT_RS the 4-wide form is used instead: it exists only with
+// stochastic rounding (.rs), whose rounding bits come from `rbits`. Measured
+// on B200: the 32 bits act as two 16-bit values, one per output pair, and
+// within a pair the low-byte element reads them bit-reversed; 0x80018001 adds
+// half an e4m3 ulp (plus 2^-16 ulp) to each element before truncation, i.e.
+// round-to-nearest with ties away from zero — identical to cvt.rn on 65536
+// sampled non-tie values. The elements go in reverse order so that `a` lands
+// in the lowest byte.
 __device__ __forceinline__ uint32_t cvt_e4m3x4(float a, float b, float c, float d) {
   uint32_t r;
+#if FA8_CVT_RS
+  asm("cvt.rs.satfinite.e4m3x4.f32 %0, {%1, %2, %3, %4}, %5;"
+      : "=r"(r)
+      : "f"(d), "f"(c), "f"(b), "f"(a), "r"(0x80018001u));
+#else
   asm("{\n .reg .b16 lo, hi;\n"
       " cvt.rn.satfinite.e4m3x2.f32 lo, %2, %1;\n"
       " cvt.rn.satfinite.e4m3x2.f32 hi, %4, %3;\n"
       " mov.b32 %0, {lo, hi};\n}"
       : "=r"(r)
       : "f"(a), "f"(b), "f"(c), "f"(d));
+#endif
   return r;
 }
 // Two e4m3 bytes (lo, hi) -> two halves.
