@@ -214,6 +214,29 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Position of K(t) / V(t) (t-th K/V tile processed, of n) in the load order
+// K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1) — the order in which the
+// MMA issuer uses them (QK(t+1) is issued before PV(t)).
+__device__ __forceinline__ int load_slot_k(int t) { return t == 0 ? 0 : 2 * t - 1; }
+__device__ __forceinline__ int load_slot_v(int t, int n) {
+  return t == n - 1 ? 2 * n - 1 : 2 * t + 2;
+}
+__device__ __forceinline__ void load_slot_inverse(int L, int n, bool& is_v, int& t) {
+  if (L == 0) {
+    is_v = false;
+    t = 0;
+  } else if (L == 2 * n - 1) {
+    is_v = true;
+    t = n - 1;
+  } else if (L & 1) {
+    is_v = false;
+    t = (L + 1) / 2;
+  } else {
+    is_v = true;
+    t = (L - 2) / 2;
+  }
+}
+
 // Number of K/V tiles query tile `i` needs, and whether its P is split.
 struct TilePlan {
   int n;       // K/V tiles (tile indices 0 .. n-1)
@@ -419,23 +442,25 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       }
       int issued = 0;
       bool ok = true;
-      for (int t = 0; t < nmax && ok; ++t) {
+      // Loads go in the order the MMA thread consumes them (K0, K1, V0, K2, V1,
+      // ..., V(n-1)), so a stage is refilled as soon as the oldest use ends.
+      for (int L = 0; L < 2 * nmax && ok; ++L) {
+        bool is_v;
+        int t;
+        load_slot_inverse(L, nmax, is_v, t);
         const int kv = nmax - 1 - t;
-        for (int part = 0; part < 2 && ok; ++part) {
-          const int L = 2 * t + part;
-          const int st = L % NS;
-          if (L >= NS) ok = bounded_wait(&bars.kv_empty[st], ((L / NS) - 1) & 1, abort_flag, p.status);
-          if (!ok) break;
-          ptx::mbar_arrive_expect_tx(&bars.kv_full[st], C::kStageBytes);
-          uint8_t* dst = smem + C::kOffRing + st * C::kStageBytes;
-          if (part == 0)
-            ptx::tma_load_4d(dst, &tm_k, &bars.kv_full[st], 0, kv_base + kv * kBlockN, hk, tb,
-                             pol_kv);
-          else
-            ptx::tma_load_4d(dst, &tm_v, &bars.kv_full[st], kv_base + kv * kBlockN, 0, hk, tb,
-                             pol_kv);
-          ++issued;
-        }
+        const int st = L % NS;
+        if (L >= NS) ok = bounded_wait(&bars.kv_empty[st], ((L / NS) - 1) & 1, abort_flag, p.status);
+        if (!ok) break;
+        ptx::mbar_arrive_expect_tx(&bars.kv_full[st], C::kStageBytes);
+        uint8_t* dst = smem + C::kOffRing + st * C::kStageBytes;
+        if (!is_v)
+          ptx::tma_load_4d(dst, &tm_k, &bars.kv_full[st], 0, kv_base + kv * kBlockN, hk, tb,
+                           pol_kv);
+        else
+          ptx::tma_load_4d(dst, &tm_v, &bars.kv_full[st], kv_base + kv * kBlockN, 0, hk, tb,
+                           pol_kv);
+        ++issued;
       }
       if (!ok) {
         // Drain: wait (bounded) for the last copies issued so that no TMA
@@ -474,7 +499,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         // S_i(t+1) = Q_i K(t+1)^T
         if (i == 0) FA8_TR(2, t + 1, 0);
         if (t + 1 < nmax) {
-          const int L = 2 * (t + 1);
+          const int L = load_slot_k(t + 1);
           const int st = L % NS;
           ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
           if (!ok) break;
@@ -503,7 +528,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         }
         // O_i += P_i(t) V(t)
         if (t >= 0) {
-          const int L = 2 * t + 1;
+          const int L = load_slot_v(t, nmax);
           const int st = L % NS;
           ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
           if (!ok) break;
