@@ -54,6 +54,8 @@ class Fa8FwdParams(C.Structure):
         ("reserved0", C.c_int32),
         ("cu_seqlens_q", C.c_void_p), ("cu_seqlens_kv", C.c_void_p),
         ("max_seqlen_q", C.c_int64),
+        ("wait_timeout_cycles", C.c_int64), ("debug_skip_kv_loads", C.c_int32),
+        ("reserved1", C.c_int32),
     ]
 
 

@@ -147,6 +147,8 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.lse_sb = p->lse_stride_b;
   kp.lse_sh = p->lse_stride_h;
   kp.status = p->status;
+  kp.timeout_cycles = p->wait_timeout_cycles > 0 ? p->wait_timeout_cycles : fa8::kTimeoutCycles;
+  kp.debug_skip_kv_loads = p->debug_skip_kv_loads;
   if (varlen) {  // sequences are addressed by their packed row offsets
     kp.o_sb = 0;
     kp.lse_sb = 0;

@@ -138,6 +138,8 @@ struct KernelParams {
   int* status;
   const int* cu_seqlens_q;   // varlen: (batch + 1) prefix sums, or null
   const int* cu_seqlens_kv;
+  long long timeout_cycles;  // bound of every barrier wait
+  int debug_skip_kv_loads;   // test hook: issue no K/V loads (waits run out)
 };
 
 #ifdef FA8_TRACE
@@ -180,7 +182,8 @@ struct Bars {
 
 // Bounded wait on phase `parity` of `bar`. Returns false on abort/timeout.
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
-                                             volatile int* abort_flag, int* status) {
+                                             volatile int* abort_flag, int* status,
+                                             long long limit) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
 #ifdef FA8_TRACE
@@ -206,7 +209,7 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
       if (ptx::mbar_try_wait(bar, parity)) return true;
 #endif
     if (*abort_flag) return false;
-    if (clock64() - t0 > kTimeoutCycles) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       if (status) atomicOr(status, 1);
       return false;
@@ -444,13 +447,13 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       bool ok = true;
       // Loads go in the order the MMA thread consumes them (K0, K1, V0, K2, V1,
       // ..., V(n-1)), so a stage is refilled as soon as the oldest use ends.
-      for (int L = 0; L < 2 * nmax && ok; ++L) {
+      for (int L = 0; L < 2 * nmax && ok && !p.debug_skip_kv_loads; ++L) {
         bool is_v;
         int t;
         load_slot_inverse(L, nmax, is_v, t);
         const int kv = nmax - 1 - t;
         const int st = L % NS;
-        if (L >= NS) ok = bounded_wait(&bars.kv_empty[st], ((L / NS) - 1) & 1, abort_flag, p.status);
+        if (L >= NS) ok = bounded_wait(&bars.kv_empty[st], ((L / NS) - 1) & 1, abort_flag, p.status, p.timeout_cycles);
         if (!ok) break;
         ptx::mbar_arrive_expect_tx(&bars.kv_full[st], C::kStageBytes);
         uint8_t* dst = smem + C::kOffRing + st * C::kStageBytes;
@@ -468,13 +471,13 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         for (int L = max(0, issued - NS); L < issued; ++L) {
           const long long t0 = clock64();
           while (!ptx::mbar_try_wait(&bars.kv_full[L % NS], (L / NS) & 1) &&
-                 clock64() - t0 < kTimeoutCycles) {
+                 clock64() - t0 < p.timeout_cycles) {
           }
         }
         for (int i = 0; i < kTilesPerCta; ++i) {
           if (tp[i].n == 0) continue;
           const long long t0 = clock64();
-          while (!ptx::mbar_try_wait(&bars.q_full[i], 0) && clock64() - t0 < kTimeoutCycles) {
+          while (!ptx::mbar_try_wait(&bars.q_full[i], 0) && clock64() - t0 < p.timeout_cycles) {
           }
         }
       }
@@ -494,20 +497,20 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       const bool active = tp[i].n > 0;
       const int role = 2 + i;
       bool ok = true;
-      if (active) ok = bounded_wait(&bars.q_full[i], 0, abort_flag, p.status);
+      if (active) ok = bounded_wait(&bars.q_full[i], 0, abort_flag, p.status, p.timeout_cycles);
       for (int t = -1; t < nmax && ok; ++t) {
         // S_i(t+1) = Q_i K(t+1)^T
         if (i == 0) FA8_TR(2, t + 1, 0);
         if (t + 1 < nmax) {
           const int L = load_slot_k(t + 1);
           const int st = L % NS;
-          ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
+          ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status, p.timeout_cycles);
           if (!ok) break;
           if (i == 0) FA8_TR(2, t + 1, 1);
           const int tl = t + 1 - start;
           if (active && tl >= 0) {
             if (tl > 0) {
-              ok = bounded_wait(&bars.s_free[i], (tl - 1) & 1, abort_flag, p.status);
+              ok = bounded_wait(&bars.s_free[i], (tl - 1) & 1, abort_flag, p.status, p.timeout_cycles);
               if (!ok) break;
             }
             ptx::tc_fence_after();
@@ -530,12 +533,12 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         if (t >= 0) {
           const int L = load_slot_v(t, nmax);
           const int st = L % NS;
-          ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status);
+          ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status, p.timeout_cycles);
           if (!ok) break;
           if (i == 0) FA8_TR(2, t + 1, 4);
           const int tl = t - start;
           if (active && tl >= 0) {
-            ok = bounded_wait(&bars.p_full[i], tl & 1, abort_flag, p.status);
+            ok = bounded_wait(&bars.p_full[i], tl & 1, abort_flag, p.status, p.timeout_cycles);
             if (!ok) break;
             ptx::tc_fence_after();
             const uint32_t v_addr = s_base + C::kOffRing + st * C::kStageBytes;
@@ -565,7 +568,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       // Drain every MMA this thread issued before TMEM is freed.
       ptx::umma_commit(&bars.drain[i]);
       const long long t0 = clock64();
-      while (!ptx::mbar_try_wait(&bars.drain[i], 0) && clock64() - t0 < kTimeoutCycles) {
+      while (!ptx::mbar_try_wait(&bars.drain[i], 0) && clock64() - t0 < p.timeout_cycles) {
       }
     }
   }
@@ -591,7 +594,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
     for (int tl = 0; tl < n && ok; ++tl) {
       const int kv = n - 1 - tl;
       if (r == 0) FA8_TR(i, tl, 0);
-      ok = bounded_wait(&bars.s_full[i], tl & 1, abort_flag, p.status);
+      ok = bounded_wait(&bars.s_full[i], tl & 1, abort_flag, p.status, p.timeout_cycles);
       if (r == 0) FA8_TR(i, tl, 1);
       if (!ok) break;
       ptx::tc_fence_after();
@@ -625,7 +628,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       if (kStaggerT && i == 1 && tl == 0) {
         // Start one exp phase behind warpgroup 0 so that one group's barrier
         // waits, S loads and P stores overlap the other's exp work.
-        ok = bounded_wait(&bars.offset, 0, abort_flag, p.status);
+        ok = bounded_wait(&bars.offset, 0, abort_flag, p.status, p.timeout_cycles);
         if (!ok) break;
       }
       StepOut so;
@@ -655,7 +658,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       // PV(t-1) must be complete before O is rescaled or P overwritten.
       if (r == 0) FA8_TR(i, tl, 3);
       if (tl > 0) {
-        ok = bounded_wait(&bars.o_done[i], (tl - 1) & 1, abort_flag, p.status);
+        ok = bounded_wait(&bars.o_done[i], (tl - 1) & 1, abort_flag, p.status, p.timeout_cycles);
         if (!ok) break;
         if (r == 0) FA8_TR(i, tl, 4);
         ptx::tc_fence_after();
@@ -698,7 +701,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
     }
     // Epilogue: O / l -> global, LSE.
     if (r == 0) FA8_TR(i, 63, 0);
-    if (n > 0 && ok) ok = bounded_wait(&bars.o_done[i], (n - 1) & 1, abort_flag, p.status);
+    if (n > 0 && ok) ok = bounded_wait(&bars.o_done[i], (n - 1) & 1, abort_flag, p.status, p.timeout_cycles);
     if (r == 0) FA8_TR(i, 63, 1);
     if (tp[i].q_start < sq) {
       ptx::tc_fence_after();

@@ -113,6 +113,15 @@ typedef struct fa8_fwd_params {
   const int32_t* cu_seqlens_q;
   const int32_t* cu_seqlens_kv;
   int64_t max_seqlen_q;
+
+  /* Failure detection. Every barrier wait inside the kernel gives up after
+   * wait_timeout_cycles SM clocks (0 = default, about two seconds); the CTA
+   * then ORs FA8_DEVERR_TIMEOUT into *status, frees its resources and exits,
+   * leaving the context usable. debug_skip_kv_loads (tests only) makes the
+   * kernel issue no K/V loads so that the waits run out. */
+  int64_t wait_timeout_cycles;
+  int32_t debug_skip_kv_loads;
+  int32_t reserved1;
 } fa8_fwd_params;
 
 /* Fill *p with defaults: contiguous strides for the given shape, scale
