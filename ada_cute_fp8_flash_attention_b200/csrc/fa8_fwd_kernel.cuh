@@ -8,13 +8,16 @@
 //   * a CTA owns T = 1 (default; two CTAs per SM) or T = 2 (one CTA per SM)
 //     128-row query tiles of one (batch, head); 128 (T + 1) threads: T softmax
 //     warpgroups and one control warpgroup; setmaxnreg gives the softmax
-//     warpgroups 200 registers per thread;
+//     warpgroups 192 (T = 1) or 200 (T = 2) registers per thread;
 //   * control warp 1 (TMA) streams K and V tiles (128 keys each) into a ring of
 //     shared-memory stages (cp.async.bulk.tensor, mbarrier completion);
 //   * control warps 0 and 2 (one elected thread each, one per query tile)
 //     issue tcgen05.mma kind::f8f6f4:
 //       S_i = Q_i K^T  into TMEM (128 lanes x 128 f32 columns per tile),
 //       O_i += P_i V   into TMEM (128 lanes x D f32 columns per tile);
+//     K/V tiles are loaded in exactly the order these products use them
+//     (K0, K1, V0, K2, V1, ...), so every ring stage is reused first-in
+//     first-out;
 //   * warps 0-3 (and 4-7) are the softmax warpgroups of Q0 (and Q1). Each thread
 //     owns one query row (one TMEM lane): row max and row sum need no
 //     shuffles. They run the online softmax in base 2 (the reference's
@@ -44,7 +47,7 @@
 //     which brings the relative error of P from 2^-4 to about 2^-8.
 //   * the row sum is accumulated from the unquantised fp32 P.
 //
-// Every mbarrier wait is bounded: after kTimeoutCycles the waiting thread
+// Every mbarrier wait is bounded: after p.timeout_cycles the waiting thread
 // raises a CTA-wide abort flag, ORs FA8_DEVERR_TIMEOUT into the optional
 // status word and all roles leave their loops, drain their in-flight
 // copies / MMAs with bounded waits, free TMEM and exit.
@@ -418,7 +421,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
   // (TMA / MMA issue) to the two softmax warpgroups; the setmaxnreg sits at
   // the top of each role's branch so the compiler sees one budget per role.
   // 128 x FA8_REGS_CONTROL + 256 x FA8_REGS_SOFTMAX must not exceed the
-  // 384 x 168 registers the CTA was launched with.
+  // registers the CTA was launched with (Roles<T>::kRegs*).
 #if FA8_REGS_CONTROL
 #define FA8_REGS_DEC() asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R::kRegsControl))
 #define FA8_REGS_INC() asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R::kRegsSoftmax))
@@ -484,7 +487,8 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
     }
   } else if (warp == kMmaWarp || (kTilesPerCta == 2 && warp == kMmaWarp2)) {
     // ------------------------------------------------------------ MMA issuers
-    // One issuing thread per query tile (warp 8: Q0, warp 10: Q1), so each
+    // One issuing thread per query tile (control warp 0: Q0, control warp 2:
+    // Q1), so each
     // tile's QK -> softmax -> PV chain advances at its own pace; the two
     // softmax warpgroups are not forced into lockstep by a shared in-order
     // issue queue. Both threads release every K/V stage (kv_empty counts 2).
