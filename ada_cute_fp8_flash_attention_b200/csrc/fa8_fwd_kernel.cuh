@@ -488,10 +488,9 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
   } else if (warp == kMmaWarp || (kTilesPerCta == 2 && warp == kMmaWarp2)) {
     // ------------------------------------------------------------ MMA issuers
     // One issuing thread per query tile (control warp 0: Q0, control warp 2:
-    // Q1), so each
-    // tile's QK -> softmax -> PV chain advances at its own pace; the two
-    // softmax warpgroups are not forced into lockstep by a shared in-order
-    // issue queue. Both threads release every K/V stage (kv_empty counts 2).
+    // Q1), so each tile's QK -> softmax -> PV chain advances at its own pace;
+    // two softmax warpgroups are not forced into lockstep by a shared in-order
+    // issue queue. Every issuer releases every K/V stage (kv_empty counts T).
     if (lane == 0) {
       const int i = (warp == kMmaWarp) ? 0 : 1;
       const uint32_t q_addr = s_base + C::kOffQ + i * C::kQBytes;
