@@ -119,6 +119,25 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
     st = make_map_u8(&tv, p->v, p->seqlen_kv, D, p->heads_kv, nb, p->v_stride_r, p->v_stride_h,
                      vsb, fa8::kBlockN, D, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
+  // O as a 4-D fp16 map {D, rows, heads, batch}, box 64 x 128, 128B swizzle.
+  CUtensorMap to;
+  memset(&to, 0, sizeof(to));
+  bool o_tma = false;
+  if (p->out_dtype == FA8_OUT_F16 && (p->o_stride_s * 2) % 16 == 0 && (p->o_stride_h * 2) % 16 == 0 &&
+      (varlen || (p->o_stride_b * 2) % 16 == 0) && p->o_stride_h > 0 && p->o_stride_s > 0) {
+    auto enc = get_encode_fn();
+    if (enc) {
+      cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)p->seqlen_q, (cuuint64_t)p->heads, nb};
+      cuuint64_t strides[3] = {(cuuint64_t)p->o_stride_s * 2, (cuuint64_t)p->o_stride_h * 2,
+                               varlen ? 16ull : (cuuint64_t)(p->o_stride_b > 0 ? p->o_stride_b * 2 : 16)};
+      cuuint32_t box[4] = {64, (cuuint32_t)fa8::kBlockM, 1, 1};
+      cuuint32_t estr[4] = {1, 1, 1, 1};
+      o_tma = enc(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, p->o, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+  }
 
   fa8::KernelParams kp;
   kp.batch = (int)p->batch;
@@ -135,6 +154,7 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.n_qblocks = (int)((rows + rows_per_cta - 1) / rows_per_cta);
   kp.cu_seqlens_q = p->cu_seqlens_q;
   kp.cu_seqlens_kv = p->cu_seqlens_kv;
+  kp.o_tma = o_tma ? 1 : 0;
   kp.scale_log2 = p->softmax_scale * p->descale_q * p->descale_k * 1.4426950408889634f;
   kp.o_scale = p->descale_v;
   kp.q_offset = p->q_offset;
@@ -155,7 +175,7 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   }
 
   dim3 grid(kp.n_qblocks, (unsigned)p->heads, (unsigned)p->batch);
-  fa8::fa8_fwd_kernel<D, T><<<grid, fa8::Roles<T>::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, kp);
+  fa8::fa8_fwd_kernel<D, T><<<grid, fa8::Roles<T>::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, to, kp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "fa8_fwd_kernel launch");

@@ -99,6 +99,10 @@ constexpr bool kStagger = FA8_STAGGER != 0;
 #ifndef FA8_REGS_CONTROL
 #define FA8_REGS_CONTROL 1  // 0 = no register reallocation between roles
 #endif
+#ifndef FA8_TMA_STORE
+#define FA8_TMA_STORE 1
+#endif
+constexpr bool kTmaStore = FA8_TMA_STORE != 0;  // fp16 O tiles leave through TMA stores
 #ifndef FA8_WAIT_SLEEP
 #define FA8_WAIT_SLEEP 20000  // suspend-time hint (ns) of mbarrier waits; 0 = spin
 #endif
@@ -141,6 +145,7 @@ struct KernelParams {
   int* status;
   const int* cu_seqlens_q;   // varlen: (batch + 1) prefix sums, or null
   const int* cu_seqlens_kv;
+  int o_tma;                 // tm_o describes O (fp16, 16-byte aligned strides)
   long long timeout_cycles;  // bound of every barrier wait
   int debug_skip_kv_loads;   // test hook: issue no K/V loads (waits run out)
 };
@@ -308,7 +313,8 @@ __device__ __forceinline__ void store_o_chunk(const KernelParams& p, char* row_p
 template <int D, int kTilesPerCta>
 __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPerCta>::kMinBlocks)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, const KernelParams p) {
+                   const __grid_constant__ CUtensorMap tm_v,
+                   const __grid_constant__ CUtensorMap tm_o, const KernelParams p) {
   using C = TileCfg<D, kTilesPerCta>;
   using R = Roles<kTilesPerCta>;
   constexpr int kMmaWarp = R::kMmaWarp;
@@ -709,22 +715,65 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
     if (tp[i].q_start < sq) {
       ptx::tc_fence_after();
       const float inv_l = (l_run > 0.f && ok) ? p.o_scale / l_run : 0.f;
-      char* row_ptr = o_head + (long long)row * p.o_ss * (p.out_e4m3 ? 1 : 2);
+      // Whole fp16 tiles go out through the TMA: each thread writes its row
+      // into the (now idle) P buffers in the 128B-swizzled box layout, one
+      // thread issues the stores. Tiles that end past the sequence (ragged /
+      // varlen) and e4m3 output take per-thread global stores.
+      const bool tma_out = kTmaStore && p.o_tma && !p.out_e4m3 && n > 0 &&
+                           tp[i].q_start + kBlockM <= sq;
+      if (tma_out) {
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        if (n > 0) {
-          uint32_t u[32];
-          ptx::tmem_ld32(t_o + c * 32, u);
-          ptx::tmem_wait_ld();
-          ptx::reg_fence32(u);
+        for (int hb = 0; hb < D / 64; ++hb) {
+          // box hb = columns [64 hb, 64 hb + 64): 128 rows x 128 B
+          const uint32_t box = s_base + C::kOffP + (hb * kTilesPerCta + i) * C::kPBytes;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(u[j]) * inv_l;
-        } else {
+          for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t u[32];
+            ptx::tmem_ld32(t_o + hb * 64 + c2 * 32, u);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence32(u);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            for (int j = 0; j < 4; ++j) {  // 4 chunks of 8 halves = 16 B
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                __half2 hv = __floats2half2_rn(__uint_as_float(u[8 * j + 2 * e]) * inv_l,
+                                               __uint_as_float(u[8 * j + 2 * e + 1]) * inv_l);
+                w[e] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+              const int chunk = c2 * 4 + j;
+              ptx::st_shared_v4(box + r * 128 + ((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+            }
+          }
         }
-        if (row < sq) store_o_chunk(p, row_ptr, c, v);
+        ptx::fence_proxy_async_smem();
+        ptx::named_barrier_sync(1 + i, kBlockM);
+        if (r == 0) {
+#pragma unroll
+          for (int hb = 0; hb < D / 64; ++hb)
+            ptx::tma_store_4d(&tm_o, smem + C::kOffP + (hb * kTilesPerCta + i) * C::kPBytes,
+                              hb * 64, q_base + tp[i].q_start, h, tb);
+          ptx::bulk_commit_group();
+          ptx::bulk_wait_group_read0();
+        }
+      } else {
+        char* row_ptr = o_head + (long long)row * p.o_ss * (p.out_e4m3 ? 1 : 2);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          if (n > 0) {
+            uint32_t u[32];
+            ptx::tmem_ld32(t_o + c * 32, u);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence32(u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(u[j]) * inv_l;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          if (row < sq) store_o_chunk(p, row_ptr, c, v);
+        }
       }
       if (lse_head && row < sq) {
         const float base = m_run - kPShift;
