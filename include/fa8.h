@@ -90,7 +90,7 @@ typedef struct fa8_fwd_params {
    * whose first row sees fewer than this many keys; -1 selects the default
    * (1024), 0 disables the split. */
   int32_t split_keys;
-  /* Upper bound on resident CTAs (0 = all SMs). */
+  /* Reserved (set to 0). */
   int32_t max_ctas;
 
   /* Per-tensor dequantisation factors of e4m3 Q, K, V (real value = code x
