@@ -87,58 +87,76 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling while the timed region runs."""
+    """SM clock / throttle-reason sampling while the timed region runs.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Polls NVML from a background thread every ~5 ms (nvidia-smi's 100 ms
+    loop would see almost nothing of a timed region of a few tens of ms);
+    falls back to nvidia-smi when NVML is unavailable.
+    """
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.rows = []
+        self._stop = None
+        self._thread = None
+        self._nvml = None
+        self._handle = None
+
+    def _open(self):
+        import pynvml
+        pynvml.nvmlInit()
+        handle = None
+        try:
+            import torch
+            props = torch.cuda.get_device_properties(self.cuda_index)
+            bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id,
+                                        props.pci_device_id)
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:  # noqa: BLE001
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+        self._nvml, self._handle = pynvml, handle
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+
+    def _loop(self):
+        nv, h = self._nvml, self._handle
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                  nv.nvmlDeviceGetPowerUsage(h) / 1000.0, get_reasons(h)))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.005)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
-        time.sleep(0.3)
+            self._open()
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001
+            self._nvml = None
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        rows = []
-        for line in (self.out or "").splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
-            except ValueError:
-                continue
-        if not rows:
+        if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        # under load = power well above idle
-        pmax = max(r[2] for r in rows)
-        loaded = [r for r in rows if r[2] > 0.5 * pmax] or rows
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3])
-                          if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded),
-                "sm_max_mhz": max(r[1] for r in loaded),
-                "power_w_max": pmax, "samples": len(loaded), "reasons": reasons}
+        reasons = sorted({name for _, _, bits in self.rows
+                          for name, bit in self.REASON_BITS.items() if bits & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows),
+                "sm_max_mhz": self.max_mhz,
+                "power_w_max": max(r[1] for r in self.rows), "samples": len(self.rows),
+                "reasons": reasons, "source": "NVML, 5 ms poll during the timed region"}
 
 
 def dist_setup(args):
