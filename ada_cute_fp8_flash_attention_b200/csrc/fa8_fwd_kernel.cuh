@@ -670,8 +670,8 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         ok = bounded_wait(&bars.o_done[i], (tl - 1) & 1, abort_flag, p.status, p.timeout_cycles);
         if (!ok) break;
         if (r == 0) FA8_TR(i, tl, 4);
-        ptx::tc_fence_after();
         if (need) {
+          ptx::tc_fence_after();  // TMEM accesses below follow the PV completion
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t u[32];
