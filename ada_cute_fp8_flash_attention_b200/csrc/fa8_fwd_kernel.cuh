@@ -103,6 +103,9 @@ constexpr bool kStagger = FA8_STAGGER != 0;
 #define FA8_TMA_STORE 1
 #endif
 constexpr bool kTmaStore = FA8_TMA_STORE != 0;  // fp16 O tiles leave through TMA stores
+#ifndef FA8_P_TMEM
+#define FA8_P_TMEM 1
+#endif
 #ifndef FA8_WAIT_SLEEP
 #define FA8_WAIT_SLEEP 20000  // suspend-time hint (ns) of mbarrier waits; 0 = spin
 #endif
@@ -128,6 +131,10 @@ struct TileCfg {
   static constexpr uint32_t kColS = 0;
   static constexpr uint32_t kColO = T * kBlockN;
   static constexpr uint32_t kTmemCols = (T == 2) ? 512 : 256;
+  // With one tile per CTA and D = 64, 64 TMEM columns are spare: P (hi, lo)
+  // lives there (32 columns each) and the PV product reads A from TMEM.
+  static constexpr bool kPInTmem = FA8_P_TMEM && T == 1 && D == 64;
+  static constexpr uint32_t kColP = kColO + D;
   static constexpr uint32_t kIdescS = ptx::idesc_e4m3_f32(kBlockM, kBlockN);
   static constexpr uint32_t kIdescO = ptx::idesc_e4m3_f32(kBlockM, D);
 };
@@ -552,17 +559,32 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
             ptx::tc_fence_after();
             const uint32_t v_addr = s_base + C::kOffRing + st * C::kStageBytes;
             const uint32_t d_tmem = tmem + C::kColO + i * D;
+            if constexpr (C::kPInTmem) {
+              const uint32_t a_hi = tmem + C::kColP;
 #pragma unroll
-            for (int kk = 0; kk < kBlockN / 32; ++kk) {
-              ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_hi + kk * 32, 128),
-                           ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO,
-                           (tl > 0 || kk > 0) ? 1u : 0u);
-            }
-            if (tp[i].split) {
+              for (int kk = 0; kk < kBlockN / 32; ++kk)
+                ptx::umma_f8_ts(d_tmem, a_hi + kk * 8,
+                                ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO,
+                                (tl > 0 || kk > 0) ? 1u : 0u);
+              if (tp[i].split) {
+#pragma unroll
+                for (int kk = 0; kk < kBlockN / 32; ++kk)
+                  ptx::umma_f8_ts(d_tmem, a_hi + 32 + kk * 8,
+                                  ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO, 1u);
+              }
+            } else {
 #pragma unroll
               for (int kk = 0; kk < kBlockN / 32; ++kk) {
-                ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_lo + kk * 32, 128),
-                             ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO, 1u);
+                ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_hi + kk * 32, 128),
+                             ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO,
+                             (tl > 0 || kk > 0) ? 1u : 0u);
+              }
+              if (tp[i].split) {
+#pragma unroll
+                for (int kk = 0; kk < kBlockN / 32; ++kk) {
+                  ptx::umma_f8(d_tmem, ptx::smem_desc_kmajor(p_lo + kk * 32, 128),
+                               ptx::smem_desc_kmajor(v_addr + kk * 32, 128), C::kIdescO, 1u);
+                }
               }
             }
             ptx::umma_commit(&bars.o_done[i]);
@@ -685,17 +707,26 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
           ptx::tmem_wait_st();
         }
       }
-      const uint32_t row_addr_hi = p_hi + r * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        ptx::st_shared_v4(row_addr_hi + ((c ^ (r & 7)) << 4), ph[4 * c], ph[4 * c + 1],
-                          ph[4 * c + 2], ph[4 * c + 3]);
-      if (split) {
-        const uint32_t row_addr_lo = p_lo + r * 128;
+      if constexpr (C::kPInTmem) {
+        // P row -> this lane's 32 TMEM columns (hi) and the next 32 (lo); the
+        // stores follow PV(t-1)'s reads of the same columns.
+        if (tl > 0 && !need) ptx::tc_fence_after();
+        ptx::tmem_st32(tmem + lane_off + C::kColP, ph);
+        if (split) ptx::tmem_st32(tmem + lane_off + C::kColP + 32, pl);
+        ptx::tmem_wait_st();
+      } else {
+        const uint32_t row_addr_hi = p_hi + r * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          ptx::st_shared_v4(row_addr_lo + ((c ^ (r & 7)) << 4), pl[4 * c], pl[4 * c + 1],
-                            pl[4 * c + 2], pl[4 * c + 3]);
+          ptx::st_shared_v4(row_addr_hi + ((c ^ (r & 7)) << 4), ph[4 * c], ph[4 * c + 1],
+                            ph[4 * c + 2], ph[4 * c + 3]);
+        if (split) {
+          const uint32_t row_addr_lo = p_lo + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            ptx::st_shared_v4(row_addr_lo + ((c ^ (r & 7)) << 4), pl[4 * c], pl[4 * c + 1],
+                              pl[4 * c + 2], pl[4 * c + 3]);
+        }
       }
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
