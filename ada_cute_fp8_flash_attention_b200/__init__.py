@@ -67,12 +67,19 @@ def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout
     ``-inf`` for rows with no visible key. ``q_offset``/``kv_offset`` are global
     positions used by the causal mask (context-parallel chunks). ``split_keys``:
     query tiles whose first row sees fewer keys than this use a two-term (hi +
-    lo) e4m3 P; -1 = default (1024), 0 = never. ``descale_q/k/v``: per-tensor
-    dequantisation factors of scaled e4m3 inputs (real value = code x factor).
+    lo) e4m3 P; -1 = default (1024), 0 = never. ``descale_q/k/v``: dequantisation
+    factors of scaled e4m3 inputs (real value = code x factor), each a float
+    (per tensor) or a device tensor that broadcasts to (B, H) for Q and to
+    (B, H_kv) for K and V (per batch and head).
     """
+    import torch
+
+    def split(d):
+        return (1.0, d) if isinstance(d, torch.Tensor) else (float(d), None)
+    (sq, tq), (sk, tk), (sv, tv) = split(descale_q), split(descale_k), split(descale_v)
     res = _C.flash_attn_fp8_forward_ex(q, k, v, causal, softmax_scale, v_layout, return_lse,
                                        out_dtype, q_offset, kv_offset, split_keys, out, lse,
-                                       descale_q, descale_k, descale_v)
+                                       sq, sk, sv, tq, tk, tv)
     return (res[0], res[1]) if return_lse else res[0]
 
 

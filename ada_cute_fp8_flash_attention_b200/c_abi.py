@@ -56,6 +56,9 @@ class Fa8FwdParams(C.Structure):
         ("max_seqlen_q", C.c_int64),
         ("wait_timeout_cycles", C.c_int64), ("debug_skip_kv_loads", C.c_int32),
         ("reserved1", C.c_int32),
+        ("descale_q_bh", C.c_void_p), ("descale_k_bh", C.c_void_p), ("descale_v_bh", C.c_void_p),
+        ("descale_q_stride_b", C.c_int64), ("descale_q_stride_h", C.c_int64),
+        ("descale_kv_stride_b", C.c_int64), ("descale_kv_stride_h", C.c_int64),
     ]
 
 

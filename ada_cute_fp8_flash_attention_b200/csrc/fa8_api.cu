@@ -169,6 +169,13 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.status = p->status;
   kp.timeout_cycles = p->wait_timeout_cycles > 0 ? p->wait_timeout_cycles : fa8::kTimeoutCycles;
   kp.debug_skip_kv_loads = p->debug_skip_kv_loads;
+  kp.dq_bh = p->descale_q_bh;
+  kp.dk_bh = p->descale_k_bh;
+  kp.dv_bh = p->descale_v_bh;
+  kp.dq_sb = p->descale_q_stride_b;
+  kp.dq_sh = p->descale_q_stride_h;
+  kp.dkv_sb = p->descale_kv_stride_b;
+  kp.dkv_sh = p->descale_kv_stride_h;
   if (varlen) {  // sequences are addressed by their packed row offsets
     kp.o_sb = 0;
     kp.lse_sb = 0;
@@ -217,6 +224,10 @@ void fa8_fwd_params_init(fa8_fwd_params* p, int64_t batch, int64_t heads, int64_
   p->descale_q = 1.0f;
   p->descale_k = 1.0f;
   p->descale_v = 1.0f;
+  p->descale_q_stride_b = heads;
+  p->descale_q_stride_h = 1;
+  p->descale_kv_stride_b = heads_kv;
+  p->descale_kv_stride_h = 1;
 }
 
 int fa8_fwd(const fa8_fwd_params* p, void* stream) {

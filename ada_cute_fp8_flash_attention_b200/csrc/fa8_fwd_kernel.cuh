@@ -155,6 +155,10 @@ struct KernelParams {
   int o_tma;                 // tm_o describes O (fp16, 16-byte aligned strides)
   long long timeout_cycles;  // bound of every barrier wait
   int debug_skip_kv_loads;   // test hook: issue no K/V loads (waits run out)
+  const float* dq_bh;        // optional per-(batch, head) dequant factors
+  const float* dk_bh;
+  const float* dv_bh;
+  long long dq_sb, dq_sh, dkv_sb, dkv_sh;
 };
 
 #ifdef FA8_TRACE
@@ -616,7 +620,11 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
     const int n = tp[i].n;
     const int row = tp[i].q_start + r;  // local query row
     const long long row_g = p.q_offset + row;
-    const float sl2 = p.scale_log2;
+    float sl2 = p.scale_log2;
+    float o_scale = p.o_scale;
+    if (p.dq_bh) sl2 *= __ldg(p.dq_bh + b * p.dq_sb + h * p.dq_sh);
+    if (p.dk_bh) sl2 *= __ldg(p.dk_bh + b * p.dkv_sb + hk * p.dkv_sh);
+    if (p.dv_bh) o_scale *= __ldg(p.dv_bh + b * p.dkv_sb + hk * p.dkv_sh);
     float m_run = -INFINITY;  // running max of s*scale*log2e
     float l_run = 0.f;
     bool ok = true;
@@ -745,7 +753,7 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
     if (r == 0) FA8_TR(i, 63, 1);
     if (tp[i].q_start < sq) {
       ptx::tc_fence_after();
-      const float inv_l = (l_run > 0.f && ok) ? p.o_scale / l_run : 0.f;
+      const float inv_l = (l_run > 0.f && ok) ? o_scale / l_run : 0.f;
       // Whole fp16 tiles go out through the TMA: each thread writes its row
       // into the (now idle) P buffers in the 128B-swizzled box layout, one
       // thread issues the stores. Tiles that end past the sequence (ragged /

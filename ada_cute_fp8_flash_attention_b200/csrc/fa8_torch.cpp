@@ -53,7 +53,10 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
                                         c10::optional<torch::Tensor> out_opt,
                                         c10::optional<torch::Tensor> lse_opt,
                                         double descale_q = 1.0, double descale_k = 1.0,
-                                        double descale_v = 1.0) {
+                                        double descale_v = 1.0,
+                                        c10::optional<torch::Tensor> descale_q_bh = c10::nullopt,
+                                        c10::optional<torch::Tensor> descale_k_bh = c10::nullopt,
+                                        c10::optional<torch::Tensor> descale_v_bh = c10::nullopt) {
   check_fp8_input(q, "q");
   check_fp8_input(k, "k");
   check_fp8_input(v, "v");
@@ -150,6 +153,23 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
   p.descale_q = static_cast<float>(descale_q);
   p.descale_k = static_cast<float>(descale_k);
   p.descale_v = static_cast<float>(descale_v);
+  // Per-(batch, head) factors: anything that broadcasts to (B, H) for Q and
+  // (B, H_kv) for K/V, materialised as contiguous fp32 on the device.
+  auto bh = [&](const c10::optional<torch::Tensor>& t, int64_t heads,
+                const char* name) -> torch::Tensor {
+    if (!t.has_value()) return torch::Tensor();
+    TORCH_CHECK(t->device() == q.device(), name, " must be on q's device");
+    return t->to(torch::kFloat32).expand({B, heads}).contiguous();
+  };
+  torch::Tensor dq = bh(descale_q_bh, H, "descale_q"), dk = bh(descale_k_bh, Hkv, "descale_k"),
+                dv = bh(descale_v_bh, Hkv, "descale_v");
+  if (dq.defined()) p.descale_q_bh = dq.data_ptr<float>();
+  if (dk.defined()) p.descale_k_bh = dk.data_ptr<float>();
+  if (dv.defined()) p.descale_v_bh = dv.data_ptr<float>();
+  p.descale_q_stride_b = H;
+  p.descale_q_stride_h = 1;
+  p.descale_kv_stride_b = Hkv;
+  p.descale_kv_stride_h = 1;
   check_status(fa8_fwd(&p, stream.stream()), "fa8_fwd");
   if (lse.defined()) return {out, lse};
   return {out};
@@ -169,13 +189,15 @@ std::vector<torch::Tensor> flash_attn_fp8_forward_ex(
     c10::optional<double> softmax_scale, std::string v_layout, bool return_lse,
     std::string out_dtype, int64_t q_offset, int64_t kv_offset, int64_t split_keys,
     c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> lse, double descale_q,
-    double descale_k, double descale_v) {
+    double descale_k, double descale_v, c10::optional<torch::Tensor> descale_q_bh,
+    c10::optional<torch::Tensor> descale_k_bh, c10::optional<torch::Tensor> descale_v_bh) {
   TORCH_CHECK(q.dim() == 4, "q must be (B, H, S, D)");
   const double scale = softmax_scale.has_value()
                            ? *softmax_scale
                            : 1.0 / std::sqrt(static_cast<double>(q.size(3)));
   return forward_impl(q, k, v, causal, scale, v_layout, return_lse, out_dtype, q_offset,
-                      kv_offset, split_keys, out, lse, descale_q, descale_k, descale_v);
+                      kv_offset, split_keys, out, lse, descale_q, descale_k, descale_v,
+                      descale_q_bh, descale_k_bh, descale_v_bh);
 }
 
 // Variable-length (packed) batches: q (total_q, H, D), k (total_kv, H_kv, D),
@@ -319,6 +341,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_dtype") = "fp16", py::arg("q_offset") = 0, py::arg("kv_offset") = 0,
         py::arg("split_keys") = -1, py::arg("out") = py::none(), py::arg("lse") = py::none(),
         py::arg("descale_q") = 1.0, py::arg("descale_k") = 1.0, py::arg("descale_v") = 1.0,
+        py::arg("descale_q_bh") = py::none(), py::arg("descale_k_bh") = py::none(),
+        py::arg("descale_v_bh") = py::none(),
         "FP8 attention forward with options; returns [out] or [out, lse]");
   m.def("flash_attn_fp8_varlen_forward", &flash_attn_fp8_varlen_forward, py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("cu_seqlens_q"), py::arg("cu_seqlens_kv"),

@@ -122,6 +122,20 @@ typedef struct fa8_fwd_params {
   int64_t wait_timeout_cycles;
   int32_t debug_skip_kv_loads;
   int32_t reserved1;
+
+  /* Per-(batch, head) dequantisation factors (optional device float arrays,
+   * NULL = 1), applied on top of the per-tensor factors: query head h of
+   * batch b uses descale_q_bh[b * descale_q_stride_b + h * descale_q_stride_h];
+   * K and V use their K/V head hk with the kv strides. A batch stride of 0
+   * shares one row of factors across the batch. For varlen calls b is the
+   * sequence index. */
+  const float* descale_q_bh;
+  const float* descale_k_bh;
+  const float* descale_v_bh;
+  int64_t descale_q_stride_b;
+  int64_t descale_q_stride_h;
+  int64_t descale_kv_stride_b;
+  int64_t descale_kv_stride_h;
 } fa8_fwd_params;
 
 /* Fill *p with defaults: contiguous strides for the given shape, scale

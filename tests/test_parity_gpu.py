@@ -169,6 +169,37 @@ def test_per_tensor_descale(fa8, cuda):
     assert np.abs(lse.cpu().numpy() - l_ref).max() < 1e-3
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_per_head_descale(fa8, cuda, D):
+    """Per-(batch, head) factors (GQA: Q per query head, K/V per kv head),
+    combined with per-tensor factors and broadcast shapes."""
+    import torch
+    from oracle import attention_ref as ref
+    B, H, Hkv, S = 2, 4, 2, 320
+    q, k, v = U.inputs(B, H, Hkv, S, S, D, "normal", 1.0, seed=23)
+    rng = np.random.default_rng(5)
+    dq = rng.uniform(0.25, 2.0, (B, H)).astype(np.float32)
+    dk = rng.uniform(0.25, 2.0, (B, Hkv)).astype(np.float32)
+    dv = rng.uniform(0.25, 2.0, (1, Hkv)).astype(np.float32)  # broadcast over batch
+    out, lse = run_ex(fa8, q, k, v, cuda, causal=True, return_lse=True,
+                      descale_q=torch.from_numpy(dq).to(cuda),
+                      descale_k=torch.from_numpy(dk).to(cuda),
+                      descale_v=torch.from_numpy(dv).to(cuda))
+    o_ref, l_ref = ref.attention(ref.e4m3_decode(q) * dq[:, :, None, None],
+                                 ref.e4m3_decode(k) * dk[:, :, None, None],
+                                 ref.e4m3_decode(v) * dv[:, :, None, None], True)
+    U.assert_close(out.float().cpu().numpy(), o_ref, max_abs=U.MAX_ABS * 2, mean_abs=U.MEAN_ABS * 2)
+    assert np.abs(lse.cpu().numpy() - l_ref).max() < 1e-3
+    # a per-tensor float on top of per-head tensors multiplies in
+    out2 = run_ex(fa8, q, k, v, cuda, causal=True, descale_q=torch.from_numpy(dq).to(cuda),
+                  descale_k=0.5, descale_v=torch.from_numpy(dv).to(cuda))
+    o_ref2, _ = ref.attention(ref.e4m3_decode(q) * dq[:, :, None, None],
+                              ref.e4m3_decode(k) * 0.5,
+                              ref.e4m3_decode(v) * dv[:, :, None, None], True)
+    U.assert_close(out2.float().cpu().numpy(), o_ref2, max_abs=U.MAX_ABS * 2,
+                   mean_abs=U.MEAN_ABS * 2)
+
+
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("D", [64, 128])
 def test_varlen_packed_sequences(fa8, cuda, causal, D):
