@@ -673,7 +673,10 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
       StepOut so;
       if (!tile_masked && !split) {
         // Hot path: an unmasked K/V tile, single-term P — no mask or split code.
-        so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, false, m_run, l_run, ph, pl);
+        // D = 128: P conversion fused into the exp loop (+0.6% on C2; D = 64
+        // measured 1% slower with it).
+        so = softmax_row_step<kBlockN, kEmuPer8, D == 128>(s, sl2, tl == 0, false, m_run, l_run,
+                                                           ph, pl);
       } else {
         // Mask: keys past seqlen_kv, and (causal) keys after this query.
         long long lim = skv - kv0;

@@ -31,6 +31,9 @@ constexpr float kPShift = 6.0f;            // log2 of the P scale-up
 constexpr float kRescaleThreshold = FA8_RESCALE_THRESHOLD;  // log2 units
 static_assert(kPShift + kRescaleThreshold <= 8.8f, "largest P must stay below e4m3's 448");
 
+#ifndef FA8_FUSED_CVT
+#define FA8_FUSED_CVT 1
+#endif
 #ifndef FA8_EMU_DEG
 #define FA8_EMU_DEG 3
 #endif
@@ -83,7 +86,8 @@ struct StepOut {
   bool need;    // warp-uniform: O must be rescaled by alpha
 };
 
-template <int NC, int kEmuPer8>
+// kFuse (callers that pass split = false): P is converted inside the exp loop.
+template <int NC, int kEmuPer8, bool kFuse = false>
 __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, bool first,
                                                     bool split, float& m_run, float& l_run,
                                                     uint32_t (&ph)[NC / 4],
@@ -133,6 +137,13 @@ __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, b
       e = ptx::pack2(s[c], s[c + 1]);
     }
     acc[(c / 2) % 4] = ptx::fadd2(acc[(c / 2) % 4], e);
+#if FA8_FUSED_CVT
+    // Without the split, each group of four is converted as soon as it is
+    // ready, so the e4m3 conversions of earlier columns overlap the ex2 of
+    // later ones instead of forming a separate phase.
+    if (kFuse && (c % 4) == 2)
+      ph[c / 4] = ptx::cvt_e4m3x4(s[c - 2], s[c - 1], s[c], s[c + 1]);
+#endif
   }
   {
     const uint64_t a01 = ptx::fadd2(acc[0], acc[1]);
@@ -147,7 +158,8 @@ __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, b
   if (!split) {
 #pragma unroll
     for (int j = 0; j < NC / 4; ++j) {
-      ph[j] = ptx::cvt_e4m3x4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
+      if (!(FA8_FUSED_CVT && kFuse))
+        ph[j] = ptx::cvt_e4m3x4(s[4 * j], s[4 * j + 1], s[4 * j + 2], s[4 * j + 3]);
       pl[j] = 0u;
     }
   } else {
