@@ -694,6 +694,12 @@ __global__ void __launch_bounds__(Roles<kTilesPerCta>::kThreads, Roles<kTilesPer
         if (lane == 0) ptx::mbar_arrive(&bars.offset);
         offset_sent = true;
       }
+#ifdef FA8_TRACE
+      if (r == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && tl < 64) {
+        fa8_trace_buf[i][tl][6] = so.t_max;  // rescale decision taken
+        fa8_trace_buf[i][tl][7] = so.t_exp;  // exponentials and row sum done
+      }
+#endif
       const bool need = so.need;
       const float alpha = so.alpha;
 

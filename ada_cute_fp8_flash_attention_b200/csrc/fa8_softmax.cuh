@@ -84,6 +84,9 @@ __device__ __forceinline__ uint64_t exp2_emu_pair(float x0, float x1) {
 struct StepOut {
   float alpha;  // factor to apply to the row's O accumulator (1 if !need)
   bool need;    // warp-uniform: O must be rescaled by alpha
+#ifdef FA8_TRACE
+  long long t_max, t_exp;  // clock64 after the rescale decision / the exp loop
+#endif
 };
 
 // kFuse (callers that pass split = false): P is converted inside the exp loop.
@@ -117,6 +120,9 @@ __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, b
   out.alpha = 1.f;
   if (out.need) out.alpha = (m_run == -INFINITY) ? 0.f : ptx::ex2(m_run - m_use);
   m_run = m_use;
+#ifdef FA8_TRACE
+  out.t_max = clock64();
+#endif
 
   // 3 + 4. exponentials and row sum
   const uint64_t sl2x2 = ptx::pack2(sl2, sl2);
@@ -152,6 +158,9 @@ __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, b
     ptx::unpack2(ptx::fadd2(a01, a23), u0, u1);
     l_run = l_run * out.alpha + (u0 + u1);
   }
+#ifdef FA8_TRACE
+  out.t_exp = clock64();
+#endif
 
   // 5. e4m3 P (hi) and, for split tiles, the e4m3 residual P - hi (lo). Two
   //    separate loops so the common (no split) path carries no branches.
