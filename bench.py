@@ -51,6 +51,12 @@ CONFIGS = {
                causal=True, dist="normal", sigma=1.0),
 }
 WORKLOAD = dict(CONFIGS["c2"], seed=1234)
+CP_DESC = {
+    "allgather": "cp{world} zig-zag chunks, async NCCL all-gather of e4m3 K/V overlapped with "
+                 "own-chunk compute, one launch per chunk pair, LSE merge",
+    "ring": "cp{world} zig-zag chunks, NCCL point-to-point ring of e4m3 K/V overlapped with "
+            "compute, one launch per chunk pair, LSE merge",
+}
 METRIC = "FP8 attn fwd TFLOPS/GPU and % of FP8 dense peak; ms/call at 1/2/4/8 B200"
 FP8_SPEC_TFLOPS = 4500.0
 
@@ -472,7 +478,7 @@ def run_context_parallel(args):
     kl = torch.cat(chunk(lambda: (B, H, c, D), 2), dim=2).to(device)
     vl = torch.cat(chunk(lambda: (B, H, D, c), 3), dim=3).to(device)
     del gen
-    step = lambda: cp.ring_attention(ql, kl, vl, zz, rank)  # noqa: E731
+    step = lambda: cp.ring_attention(ql, kl, vl, zz, rank, schedule=args.cp_schedule)  # noqa: E731
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -502,7 +508,7 @@ def run_context_parallel(args):
                 "dtype": "e4m3", "data": "synthetic",
                 "config": {"workload": W["name"], "global_batch": B, "seq_len": S,
                            "heads": H, "head_dim": D, "causal": True,
-                           "parallelism": f"cp{world} zig-zag chunks, async NCCL all-gather of e4m3 K/V overlapped with own-chunk compute, LSE merge"},
+                           "parallelism": CP_DESC[args.cp_schedule].format(world=world)},
                 "tflops_per_gpu": value / world,
                 "pct_fp8_spec_peak": 100.0 * value / world / FP8_SPEC_TFLOPS,
                 "pct_fp8_2x_measured_bf16": 100.0 * value / world / (2 * bf16),
@@ -524,6 +530,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e arm")
     ap.add_argument("--workload", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--cp-schedule", default="allgather", choices=["allgather", "ring"],
+                    help="K/V exchange of the context-parallel workload (c5)")
     ap.add_argument("--shape", default=None,
                     help="B,H,S,D,causal override for profiling runs (not a bench line)")
     args = ap.parse_args()
