@@ -9,10 +9,13 @@ compile flags that setup.py:47-66 lists, but targets ``compute_100a/sm_100a``
 instead of ``sm_89`` (setup.py:19-20). Its Ada ``mma.sync`` code compiles and
 runs on B200 unchanged (legacy tensor-core path).
 
-The result is used only as a checker: tests compare the reference kernel with
-``oracle.attention_ref.reference_kernel_semantics`` and with this project's
-kernel at the reference's effective softmax scale. Nothing in the product
-imports it. Outputs go to oracle/_ref/ (git-ignored, shipped with the tree).
+Do not run the result on a GPU. On B200 it faulted with an illegal memory
+access on a repeat call at test.py's shape: for the first query block it
+prefetches K/V tile -1 (csrc/flash_attention.cu:260-268), reading 64 rows
+before the first (batch, head)'s K and V^T, which faults whenever nothing is
+mapped in front of the allocation. It is built (and importable with load())
+only as a record of the reference's code path; no test, bench leg or product
+code calls it. Outputs go to oracle/_ref/ (git-ignored).
 
 Usage: python oracle/build_ref.py [/path/to/reference]
 """
