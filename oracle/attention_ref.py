@@ -19,8 +19,8 @@ What it restates (Lemon7-UP/ada_cute_fp8_flash_attention):
   (csrc/flash_attention.cu:90-460): causal only, effective natural-log scale
   ln(2)/sqrt(D) because ``softmax_scale`` instead of ``softmax_scale_log2``
   feeds exp2 (:307, :385, :483-484), P requantised to e4m3 unscaled
-  (:312-320), and O rounded to e4m3 (:433-441). Used to compare against the
-  reference binary rebuilt for sm_100a.
+  (:312-320), and O rounded to e4m3 (:433-441). A model of the reference's
+  documented behaviour (the reference binary itself is not run on the GPU).
 * ``e4m3_decode`` / ``e4m3_encode``: the OCP FP8 E4M3 ("fn") format the
   reference reads through ``cutlass::float_e4m3_t`` (csrc/flash_attention.cu:535)
   and torch's ``float8_e4m3fn``: 1 sign bit, 4 exponent bits (bias 7),
