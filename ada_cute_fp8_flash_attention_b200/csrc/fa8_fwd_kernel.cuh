@@ -23,7 +23,8 @@
 //     shuffles. They run the online softmax in base 2 (the reference's
 //     softmax_rescale_o, csrc/flash_attention.cu:54-88, with the scale fixed
 //     to softmax_scale * log2(e)), requantise P to e4m3 into a 128B-swizzled
-//     shared tile for the PV product, rescale O in TMEM only when the row max
+//     shared tile for the PV product (D = 64 with T = 1: into spare TMEM
+//     columns, read by the PV product from TMEM), rescale O in TMEM only when the row max
 //     grew by more than kRescaleThreshold (lazy rescale), and finally
 //     normalise O by the row sum (the reference's final_softmax_rescale_o,
 //     csrc/flash_attention.cu:38-52) and store it.
