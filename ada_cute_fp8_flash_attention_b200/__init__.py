@@ -85,18 +85,21 @@ def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout
 
 def flash_attn_fp8_varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_kv, max_seqlen_q,
                                   causal=True, softmax_scale=None, v_layout="thd",
-                                  return_lse=False, out_dtype="fp16"):
+                                  return_lse=False, out_dtype="fp16", status=None):
     """FP8 attention over packed variable-length sequences.
 
-    q: (total_q, H, D), k: (total_kv, H_kv, D), v: (total_kv, H_kv, D) ("thd") or
-    (H_kv, D, total_kv) ("hdt"), all e4m3; cu_seqlens_*: int32 prefix sums (batch+1).
-    Every cu_seqlens_kv entry must be a multiple of 16. The cu_seqlens are read on
-    the host for validation (one device-to-host copy when they live on the GPU).
+    q: (total_q, H, D), k: (total_kv, H_kv, D), v: (total_kv, H_kv, D) ("thd", read
+    in place) or (H_kv, D, total_kv) ("hdt"), all e4m3; cu_seqlens_*: int32 prefix
+    sums (batch+1) on q's device. Every cu_seqlens_kv entry must be a multiple of 16.
+    The offsets are never read on the host (no device synchronisation): the kernel
+    refuses a sequence that breaks the rules, leaves it unwritten and ORs a bit into
+    ``status`` (optional int32 device tensor): 2 = unaligned K/V start, 4 = offsets
+    outside the packed tensors or a sequence longer than ``max_seqlen_q``.
     Returns out (total_q, H, D) or (out, lse (H, total_q)).
     """
     res = _C.flash_attn_fp8_varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_kv,
                                            int(max_seqlen_q), causal, softmax_scale, v_layout,
-                                           return_lse, out_dtype)
+                                           return_lse, out_dtype, status)
     return (res[0], res[1]) if return_lse else res[0]
 
 

@@ -15,8 +15,13 @@ The reference runs one sequence on one GPU only; for the long-context shape
 * each (Q chunk, K/V chunk) pair yields a partial output normalised over that
   K/V chunk and its log-sum-exp; pairs that the causal mask removes entirely
   are skipped on the host;
-* the partials of a Q chunk are combined by log-sum-exp
-  (fa8_lse_merge: o = sum_i exp(lse_i - lse) o_i).
+* each partial output is kept in fp32 (the kernel's fp32 output mode) and
+  the partials of a Q chunk are combined by log-sum-exp
+  (fa8_lse_merge: o = sum_i exp(lse_i - lse) o_i), so no partial is rounded
+  to fp16 before the merge;
+* every wait on the K/V exchange has a host deadline: the waiting rank polls
+  the NCCL (or gloo) work objects and raises CPTimeoutError once the deadline
+  passes, instead of blocking forever on a rank that stopped sending.
 
 K/V travel as e4m3 (2 x S/(2W) x D bytes per head per step); nothing is
 loaded across GPUs by the kernels themselves (no peer-memory TMA).
@@ -27,8 +32,49 @@ CUDA kernels and there is no CPU fallback on the product path.
 """
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass
 from typing import Callable, List, Optional, Sequence, Tuple
+
+# The LSE merge takes at most this many partial outputs per query chunk; rank
+# 0's late chunk collects 2 W of them, so W <= 8.
+MAX_MERGE_PARTS = 16
+DEFAULT_DEADLINE_S = 120.0
+
+
+class CPTimeoutError(RuntimeError):
+    """A K/V exchange of the context-parallel ring did not complete in time."""
+
+
+def wait_works(works, deadline_s: Optional[float], what: str = "K/V exchange") -> None:
+    """Wait for async collective work objects with a host deadline.
+
+    Each work is waited on with the time left until the deadline
+    (``Work.wait(timeout=...)``: NCCL then blocks the host until the operation
+    completed, gloo until its data arrived, and both raise when the time runs
+    out or the peer failed); a timeout becomes CPTimeoutError.
+    ``deadline_s=None`` waits without a bound (NCCL: the caller's stream is
+    only ordered after the operation).
+    """
+    if deadline_s is None:
+        for w in works:
+            w.wait()
+        return
+    from datetime import timedelta
+    t_end = time.monotonic() + deadline_s
+    for i, w in enumerate(works):
+        left = t_end - time.monotonic()
+        if left <= 0:
+            raise CPTimeoutError(f"context parallel: {what} not complete after "
+                                 f"{deadline_s:.1f} s ({len(works) - i} operations pending)")
+        try:
+            w.wait(timeout=timedelta(seconds=left))
+        except RuntimeError as e:  # gloo / NCCL report timeouts (and peer loss) this way
+            if time.monotonic() >= t_end - 1e-3 or "timed out" in str(e).lower() or \
+                    "timeout" in str(e).lower():
+                raise CPTimeoutError(f"context parallel: {what} not complete after "
+                                     f"{deadline_s:.1f} s: {e}") from e
+            raise
 
 
 @dataclass(frozen=True)
@@ -89,9 +135,10 @@ def _default_compute(softmax_scale: Optional[float]):
     from . import flash_attn_fp8_forward_ex
 
     def compute(q, k, v_bhds, q_off, kv_off):
+        # fp32 partial output: rounded only once, by the merge
         return flash_attn_fp8_forward_ex(q, k, v_bhds, causal=True, softmax_scale=softmax_scale,
-                                         v_layout="bhds", return_lse=True, q_offset=q_off,
-                                         kv_offset=kv_off)
+                                         v_layout="bhds", return_lse=True, out_dtype="fp32",
+                                         q_offset=q_off, kv_offset=kv_off)
     return compute
 
 
@@ -103,7 +150,8 @@ def _default_merge(outs, lses):
 def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
                    softmax_scale: Optional[float] = None,
                    compute: Optional[ComputeFn] = None, merge: Optional[MergeFn] = None,
-                   schedule: str = "allgather"):
+                   schedule: str = "allgather",
+                   deadline_s: Optional[float] = DEFAULT_DEADLINE_S):
     """Causal attention of this rank's zig-zag Q chunks against the whole sequence.
 
     q_loc, k_loc: (B, H, 2*chunk, D) e4m3 — this rank's chunks (split_local, dim 2);
@@ -116,14 +164,22 @@ def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
     remaining pairs. On 8 B200s NCCL point-to-point between ring neighbours ran
     at about 80 GB/s per GPU while the all-gather moves the same bytes at
     collective bandwidth, so "allgather" is the faster schedule there.
+
+    deadline_s bounds every wait on the exchange (CPTimeoutError after it);
+    None waits without a bound.
     """
     import torch
     import torch.distributed as dist
 
+    if 2 * zz.world > MAX_MERGE_PARTS:
+        raise ValueError(f"context parallel supports at most {MAX_MERGE_PARTS // 2} ranks "
+                         f"(rank 0 merges 2 x world partial outputs, the merge takes "
+                         f"{MAX_MERGE_PARTS}); got world = {zz.world}")
     compute = compute or _default_compute(softmax_scale)
     merge = merge or _default_merge
     if schedule == "allgather":
-        return _allgather_attention(q_loc, k_loc, v_loc_bhds, zz, rank, group, compute, merge)
+        return _allgather_attention(q_loc, k_loc, v_loc_bhds, zz, rank, group, compute, merge,
+                                    deadline_s)
     if schedule != "ring":
         raise ValueError(f"unknown schedule {schedule!r}")
     W, c = zz.world, zz.chunk
@@ -157,8 +213,7 @@ def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
                 o, l = compute(q_parts[qi], k_blk, v_blk, zz.start(qc), zz.start(kc))
                 partial_o[qi].append(o)
                 partial_l[qi].append(l)
-        for r in reqs:
-            r.wait()
+        wait_works(reqs, deadline_s, f"ring step {step} (from rank {recv_from})")
         if step + 1 < W:
             cur_k, nxt_k = nxt_k, cur_k
             cur_v, nxt_v = nxt_v, cur_v
@@ -170,7 +225,8 @@ def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
     return torch.cat(outs, dim=2), torch.cat(lses, dim=2)
 
 
-def _allgather_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group, compute, merge):
+def _allgather_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group, compute, merge,
+                         deadline_s=None):
     import torch
     import torch.distributed as dist
 
@@ -210,8 +266,7 @@ def _allgather_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group,
                 partial_l[qi].append(l)
 
     run_pairs(rank, k_loc, v_loc)          # own chunks while the gather runs
-    for w in works:
-        w.wait()
+    wait_works(works, deadline_s, "K/V all-gather")
     for step in range(1, W):
         src = zz.source_rank(rank, step)
         run_pairs(src, k_all[src], v_all[src])

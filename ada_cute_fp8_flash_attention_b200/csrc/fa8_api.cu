@@ -75,15 +75,15 @@ int make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t row
   return FA8_OK;
 }
 
-template <int D, int T>
+template <int D>
 int setup_kernel_attr(int dev) {
   static std::once_flag flags[64];
   static cudaError_t errs[64];
   if (dev < 0 || dev >= 64) return set_msg(FA8_ERR_INVALID_ARG, "device index out of range");
   std::call_once(flags[dev], [dev] {
-    errs[dev] = cudaFuncSetAttribute(fa8::fa8_fwd_kernel<D, T>,
+    errs[dev] = cudaFuncSetAttribute(fa8::fa8_fwd_kernel<D>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     fa8::TileCfg<D, T>::kSmemAlloc);
+                                     fa8::TileCfg<D>::kSmemAlloc);
   });
   if (errs[dev] != cudaSuccess) return set_cuda_error(errs[dev], "cudaFuncSetAttribute");
   return FA8_OK;
@@ -91,10 +91,10 @@ int setup_kernel_attr(int dev) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <int D, int T>
+template <int D>
 int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
-  using C = fa8::TileCfg<D, T>;
-  int st = setup_kernel_attr<D, T>(dev);
+  using C = fa8::TileCfg<D>;
+  int st = setup_kernel_attr<D>(dev);
   if (st) return st;
   const CUtensorMapSwizzle swz_qk =
       (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -114,10 +114,15 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
     st = make_map_u8(&tk, p->k, D, p->seqlen_kv, p->heads_kv, nb, p->k_stride_s, p->k_stride_h,
                      ksb, D, fa8::kBlockN, swz_qk);
   if (st) return st;
-  // V^T (BHDS): innermost = keys, rows = d.
-  if (p->seqlen_kv > 0)
+  // V^T (BHDS): innermost = keys, rows = d. V (BHSD): innermost = d, rows =
+  // keys — a V tile is then shaped and swizzled like a K tile.
+  const bool v_bhsd = p->v_layout == FA8_V_BHSD;
+  if (p->seqlen_kv > 0 && !v_bhsd)
     st = make_map_u8(&tv, p->v, p->seqlen_kv, D, p->heads_kv, nb, p->v_stride_r, p->v_stride_h,
                      vsb, fa8::kBlockN, D, CU_TENSOR_MAP_SWIZZLE_128B);
+  else if (p->seqlen_kv > 0)
+    st = make_map_u8(&tv, p->v, D, p->seqlen_kv, p->heads_kv, nb, p->v_stride_r, p->v_stride_h,
+                     vsb, D, fa8::kBlockN, swz_qk);
   if (st) return st;
   // O as a 4-D fp16 map {D, rows, heads, batch}, box 64 x 128, 128B swizzle.
   CUtensorMap to;
@@ -147,14 +152,16 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.seqlen_kv = (int)p->seqlen_kv;
   kp.head_group = (int)(p->heads / p->heads_kv);
   kp.causal = p->causal ? 1 : 0;
-  kp.out_e4m3 = p->out_dtype == FA8_OUT_E4M3 ? 1 : 0;
+  kp.out_kind = p->out_dtype;
+  kp.o_esize = p->out_dtype == FA8_OUT_E4M3 ? 1 : (p->out_dtype == FA8_OUT_F32 ? 4 : 2);
   kp.split_keys = p->split_keys < 0 ? fa8::kDefaultSplitKeys : p->split_keys;
-  const int rows_per_cta = T * fa8::kBlockM;
+  const int rows_per_cta = fa8::kBlockM;
   const int64_t rows = varlen ? p->max_seqlen_q : p->seqlen_q;
   kp.n_qblocks = (int)((rows + rows_per_cta - 1) / rows_per_cta);
   kp.cu_seqlens_q = p->cu_seqlens_q;
   kp.cu_seqlens_kv = p->cu_seqlens_kv;
   kp.o_tma = o_tma ? 1 : 0;
+  kp.v_bhsd = v_bhsd ? 1 : 0;
   kp.scale_log2 = p->softmax_scale * p->descale_q * p->descale_k * 1.4426950408889634f;
   kp.o_scale = p->descale_v;
   kp.q_offset = p->q_offset;
@@ -182,7 +189,7 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   }
 
   dim3 grid(kp.n_qblocks, (unsigned)p->heads, (unsigned)p->batch);
-  fa8::fa8_fwd_kernel<D, T><<<grid, fa8::Roles<T>::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, to, kp);
+  fa8::fa8_fwd_kernel<D><<<grid, fa8::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, to, kp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "fa8_fwd_kernel launch");
@@ -236,10 +243,10 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
     return set_msg(FA8_ERR_INVALID_ARG, "negative size");
   if (p->head_dim != 64 && p->head_dim != 128)
     return set_msg(FA8_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
-  if (p->v_layout != FA8_V_BHDS)
-    return set_msg(FA8_ERR_UNSUPPORTED, "only the BHDS (pre-transposed) V layout is supported");
-  if (p->out_dtype != FA8_OUT_F16 && p->out_dtype != FA8_OUT_E4M3)
-    return set_msg(FA8_ERR_INVALID_ARG, "out_dtype must be FA8_OUT_F16 or FA8_OUT_E4M3");
+  if (p->v_layout != FA8_V_BHDS && p->v_layout != FA8_V_BHSD)
+    return set_msg(FA8_ERR_INVALID_ARG, "v_layout must be FA8_V_BHDS or FA8_V_BHSD");
+  if (p->out_dtype != FA8_OUT_F16 && p->out_dtype != FA8_OUT_E4M3 && p->out_dtype != FA8_OUT_F32)
+    return set_msg(FA8_ERR_INVALID_ARG, "out_dtype must be FA8_OUT_F16, FA8_OUT_E4M3 or FA8_OUT_F32");
   if (p->batch == 0 || p->heads == 0 || p->seqlen_q == 0) return FA8_OK;
   if (p->cu_seqlens_q || p->cu_seqlens_kv) {
     if (!p->cu_seqlens_q || !p->cu_seqlens_kv)
@@ -264,7 +271,7 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
   if (!aligned16(p->q) || !aligned16(p->o) ||
       (p->seqlen_kv > 0 && (!aligned16(p->k) || !aligned16(p->v))))
     return set_msg(FA8_ERR_ALIGNMENT, "tensor base addresses must be 16-byte aligned");
-  const int64_t osz = p->out_dtype == FA8_OUT_E4M3 ? 1 : 2;
+  const int64_t osz = p->out_dtype == FA8_OUT_E4M3 ? 1 : (p->out_dtype == FA8_OUT_F32 ? 4 : 2);
   const int64_t s16[] = {p->q_stride_b, p->q_stride_h, p->q_stride_s, p->k_stride_b,
                          p->k_stride_h, p->k_stride_s, p->v_stride_b, p->v_stride_h,
                          p->v_stride_r};
@@ -275,6 +282,9 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
       return set_msg(FA8_ERR_ALIGNMENT,
                      "Q/K/V strides must be positive multiples of 16 elements (TMA); for BHDS V "
                      "this means seqlen_kv % 16 == 0");
+  }
+  if (p->v_layout == FA8_V_BHSD && p->seqlen_kv > 0 && p->v_stride_r < p->head_dim) {
+    return set_msg(FA8_ERR_INVALID_ARG, "BHSD V rows overlap (v_stride_r < head_dim)");
   }
   if ((p->o_stride_s * osz) % 16 || (p->o_stride_h * osz) % 16 || (p->o_stride_b * osz) % 16)
     return set_msg(FA8_ERR_ALIGNMENT, "O strides must be multiples of 16 bytes");
@@ -288,15 +298,7 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
     return set_msg(FA8_ERR_NO_DEVICE, "the current device is not sm_100 (B200)");
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // Query tiles per CTA: 1 (two CTAs per SM, measured faster on every
-  // configuration) unless FA8_TILES=2 is set in the environment.
-  static int tiles_env = [] {
-    const char* e = getenv("FA8_TILES");
-    return e ? atoi(e) : 0;
-  }();
-  const int tiles = (tiles_env == 1 || tiles_env == 2) ? tiles_env : 1;
-  if (p->head_dim == 128) return tiles == 1 ? launch<128, 1>(p, s, dev) : launch<128, 2>(p, s, dev);
-  return tiles == 1 ? launch<64, 1>(p, s, dev) : launch<64, 2>(p, s, dev);
+  return p->head_dim == 128 ? launch<128>(p, s, dev) : launch<64>(p, s, dev);
 }
 
 const char* fa8_status_string(int status) {
@@ -321,12 +323,6 @@ uint64_t fa8_launch_count(void) { return g_launches.load(std::memory_order_relax
 #ifdef FA8_TRACE
 extern "C" int fa8_trace_cta_fetch(long long* host_buf) {
   return cudaMemcpyFromSymbol(host_buf, fa8::fa8_trace_cta, sizeof(fa8::fa8_trace_cta)) ==
-                 cudaSuccess
-             ? 0
-             : 1;
-}
-extern "C" int fa8_trace_spin_fetch(unsigned long long* host_buf) {
-  return cudaMemcpyFromSymbol(host_buf, fa8::fa8_trace_spin, sizeof(fa8::fa8_trace_spin)) ==
                  cudaSuccess
              ? 0
              : 1;

@@ -11,7 +11,8 @@
 //
 // Both are HBM-bound elementwise passes: 16-byte vector accesses, one
 // thread per 8 (merge) or 16 (quantise) output elements, grids sized in
-// multiples of the SM count via grid-stride loops.
+// multiples of the SM count via grid-stride loops; the transposing quantise
+// moves 64 x 64 tiles through shared memory with 16-byte global accesses.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -131,7 +132,67 @@ __global__ void quantize_kernel(const void* x, int dt, uint8_t* y, int64_t n16, 
   }
 }
 
-// Transposing quantise through a 64x64 shared tile: x[b][r][c] -> y[b][c][r].
+// Transposing quantise of whole 64 x 64 tiles with 16-byte global accesses on
+// both sides: x[b][r][c] (fp16/bf16, cols % 8 == 0) -> y[b][c][r] (e4m3, rows
+// % 16 == 0). Each thread loads 8 consecutive input elements of one row (16 B),
+// quantises them and scatters the 8 bytes into a transposed shared tile; after
+// the barrier each thread writes 16 consecutive output bytes of one output row.
+__global__ void quantize_transpose_vec_kernel(const void* x, int dt, uint8_t* y, int64_t rows,
+                                              int64_t cols, float scale) {
+  constexpr int kPad = 16;  // row pitch 80 B: keeps the 16-byte reads aligned
+  __shared__ __align__(16) uint8_t tile_t[64][64 + kPad];  // [c][r]
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
+  const int64_t base = b * rows * cols;
+  // 64 rows x 8 vectors of 8 elements = 512 vectors, two per thread.
+  for (int e = threadIdx.x; e < 512; e += blockDim.x) {
+    const int rr = e / 8, cv = (e % 8) * 8;
+    const int64_t r = r0 + rr, c = c0 + cv;
+    float v[8];
+    if (r < rows && c < cols) {  // cols % 8 == 0: the vector is all in or all out
+      const uint4 raw = *reinterpret_cast<const uint4*>(
+          static_cast<const char*>(x) + (base + r * cols + c) * 2);
+      if (dt == 0) {
+        const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(h[k]);
+          v[2 * k] = f.x;
+          v[2 * k + 1] = f.y;
+        }
+      } else {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h[k]);
+          v[2 * k] = f.x;
+          v[2 * k + 1] = f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      const uint16_t two = fa8::ptx::cvt_e4m3x2(v[k] * scale, v[k + 1] * scale);
+      tile_t[cv + k][rr] = (uint8_t)(two & 0xffu);
+      tile_t[cv + k + 1][rr] = (uint8_t)(two >> 8);
+    }
+  }
+  __syncthreads();
+  // 64 output rows x 4 vectors of 16 bytes = 256 vectors, one per thread.
+  for (int e = threadIdx.x; e < 256; e += blockDim.x) {
+    const int cc = e / 4, rv = (e % 4) * 16;
+    const int64_t c = c0 + cc, r = r0 + rv;
+    if (c < cols && r < rows)  // rows % 16 == 0: the vector is all in or all out
+      *reinterpret_cast<uint4*>(y + base + c * rows + r) =
+          *reinterpret_cast<const uint4*>(&tile_t[cc][rv]);
+  }
+}
+
+// Transposing quantise through a 64x64 shared tile, one element per access:
+// the fallback for shapes or pointers the vector kernel cannot take.
 __global__ void quantize_transpose_kernel(const void* x, int dt, uint8_t* y, int64_t rows,
                                           int64_t cols, float scale) {
   __shared__ uint8_t tile[64][64 + 4];
@@ -180,7 +241,12 @@ extern "C" int fa8_lse_merge(int n_parts, const void* const* o_parts, int o_is_f
     a.lse[i] = i < n_parts ? lse_parts[i] : nullptr;
     if (i < n_parts && (!a.o[i] || !a.lse[i]))
       return fa8_note_error(FA8_ERR_INVALID_ARG, "fa8_lse_merge: null part");
+    // Parts are read and O is written with 16-byte vector accesses.
+    if (i < n_parts && (reinterpret_cast<uintptr_t>(a.o[i]) & 15))
+      return fa8_note_error(FA8_ERR_ALIGNMENT, "fa8_lse_merge: o_parts must be 16-byte aligned");
   }
+  if (reinterpret_cast<uintptr_t>(o_out) & 15)
+    return fa8_note_error(FA8_ERR_ALIGNMENT, "fa8_lse_merge: o_out must be 16-byte aligned");
   const int64_t total = rows * (head_dim / 8);
   const int threads = 256;
   int64_t blocks = (total + threads - 1) / threads;
@@ -217,8 +283,15 @@ extern "C" int fa8_quantize_e4m3(const void* x, int in_dtype, void* y, int64_t b
     if (batch > 65535 || (rows + 63) / 64 > 65535)
       return fa8_note_error(FA8_ERR_UNSUPPORTED, "fa8_quantize_e4m3: transpose grid too large");
     dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64), (unsigned)batch);
-    quantize_transpose_kernel<<<grid, 256, 0, s>>>(x, in_dtype, static_cast<uint8_t*>(y), rows,
-                                                   cols, scale);
+    const bool vec = rows % 16 == 0 && cols % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    if (vec)
+      quantize_transpose_vec_kernel<<<grid, 256, 0, s>>>(x, in_dtype, static_cast<uint8_t*>(y),
+                                                         rows, cols, scale);
+    else
+      quantize_transpose_kernel<<<grid, 256, 0, s>>>(x, in_dtype, static_cast<uint8_t*>(y),
+                                                     rows, cols, scale);
   }
   fa8_note_launch();
   cudaError_t e = cudaGetLastError();

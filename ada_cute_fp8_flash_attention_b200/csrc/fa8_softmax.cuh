@@ -90,11 +90,17 @@ struct StepOut {
 };
 
 // kFuse (callers that pass split = false): P is converted inside the exp loop.
-template <int NC, int kEmuPer8, bool kFuse = false>
+// kStream (with kFuse): each 16-byte chunk of the e4m3 row is also stored to
+// shared memory as soon as it is converted, at p_row + ((chunk ^ swz) << 4)
+// (the 128B-swizzled row layout of the PV product's A operand), so the
+// stores overlap the rest of the exp loop.
+template <int NC, int kEmuPer8, bool kFuse = false, bool kStream = false>
 __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, bool first,
                                                     bool split, float& m_run, float& l_run,
                                                     uint32_t (&ph)[NC / 4],
-                                                    uint32_t (&pl)[NC / 4]) {
+                                                    uint32_t (&pl)[NC / 4],
+                                                    uint32_t p_row = 0, uint32_t swz = 0) {
+  static_assert(!kStream || (kFuse && NC == 128), "streamed P stores need the fused loop");
   static_assert(NC % 16 == 0, "row length must be a multiple of 16");
   // 1. row max
   constexpr int G = NC / 16;
@@ -149,6 +155,9 @@ __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, b
     // later ones instead of forming a separate phase.
     if (kFuse && (c % 4) == 2)
       ph[c / 4] = ptx::cvt_e4m3x4(s[c - 2], s[c - 1], s[c], s[c + 1]);
+    if (kStream && (c % 16) == 14)
+      ptx::st_shared_v4(p_row + (((uint32_t)(c / 16) ^ swz) << 4), ph[c / 4 - 3], ph[c / 4 - 2],
+                        ph[c / 4 - 1], ph[c / 4]);
 #endif
   }
   {

@@ -63,7 +63,8 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
   TORCH_CHECK(k.device() == q.device() && v.device() == q.device(),
               "q, k, v must be on the same device");
   TORCH_CHECK(v_layout == "bhds" || v_layout == "bhsd", "v_layout must be 'bhds' or 'bhsd'");
-  TORCH_CHECK(out_dtype == "fp16" || out_dtype == "e4m3", "out_dtype must be 'fp16' or 'e4m3'");
+  TORCH_CHECK(out_dtype == "fp16" || out_dtype == "e4m3" || out_dtype == "fp32",
+              "out_dtype must be 'fp16', 'e4m3' or 'fp32'");
   const int64_t B = q.size(0), H = q.size(1), Sq = q.size(2), D = q.size(3);
   const int64_t Hkv = k.size(1), Skv = k.size(2);
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128, got ", D);
@@ -72,46 +73,51 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
   c10::cuda::CUDAGuard guard(q.device());
   auto stream = at::cuda::getCurrentCUDAStream(q.get_device());
 
-  // V as (B, H_kv, D, S_pad) with S_pad % 16 == 0 (TMA row stride rule).
+  // V goes to the kernel as given: (B, H_kv, D, S) ("bhds", the reference's
+  // pre-transposed layout) or (B, H_kv, S, D) ("bhsd", read by the PV product
+  // as an MN-major operand). Only layouts the TMA cannot describe (a BHDS row
+  // of S_kv % 16 != 0 keys, unaligned strides) are copied first.
   torch::Tensor vt;
+  int v_code = FA8_V_BHDS;
   if (v_layout == "bhds") {
     TORCH_CHECK(v.size(0) == B && v.size(1) == Hkv && v.size(2) == D && v.size(3) == Skv,
                 "v (bhds) must be (B, H_kv, D, S_kv)");
     vt = v;
+    if (Skv % 16 != 0 || !tma_ok(vt) || vt.stride(3) != 1) {
+      const int64_t Sp = (Skv + 15) / 16 * 16;
+      auto vp = torch::empty({B, Hkv, D, Sp}, vt.options());
+      vp.narrow(3, Skv, Sp - Skv).zero_();
+      vp.narrow(3, 0, Skv).copy_(vt);
+      vt = vp;
+    }
   } else {
     TORCH_CHECK(v.size(0) == B && v.size(1) == Hkv && v.size(2) == Skv && v.size(3) == D,
                 "v (bhsd) must be (B, H_kv, S_kv, D)");
-    vt = v.transpose(2, 3);
-  }
-  if (Skv % 16 != 0 || !tma_ok(vt) || vt.stride(3) != 1) {
-    const int64_t Sp = (Skv + 15) / 16 * 16;
-    auto vp = torch::zeros({B, Hkv, D, Sp}, vt.options());
-    vp.narrow(3, 0, Skv).copy_(vt);
-    vt = vp;
+    vt = tma_ok(v) && v.stride(3) == 1 ? v : v.contiguous();
+    v_code = FA8_V_BHSD;
   }
   if (!tma_ok(q)) q = q.contiguous();
   if (!tma_ok(k)) k = k.contiguous();
 
-  const bool e4m3_out = out_dtype == "e4m3";
+  const at::ScalarType out_st = out_dtype == "e4m3"   ? at::ScalarType::Float8_e4m3fn
+                                : out_dtype == "fp32" ? at::ScalarType::Float
+                                                      : at::ScalarType::Half;
   torch::Tensor out;
   if (out_opt.has_value()) {
     out = *out_opt;
     TORCH_CHECK(out.device() == q.device(), "out must be on q's device");
-    TORCH_CHECK(out.scalar_type() ==
-                    (e4m3_out ? at::ScalarType::Float8_e4m3fn : at::ScalarType::Half),
-                "out has the wrong dtype");
+    TORCH_CHECK(out.scalar_type() == out_st, "out has the wrong dtype");
     TORCH_CHECK(out.dim() == 4 && out.size(0) == B && out.size(1) == H && out.size(2) == Sq &&
                     out.size(3) == D && out.stride(3) == 1,
                 "out must be (B, H, S_q, D) with unit last stride");
   } else {
-    out = torch::empty({B, H, Sq, D},
-                       q.options().dtype(e4m3_out ? at::ScalarType::Float8_e4m3fn
-                                                  : at::ScalarType::Half));
+    out = torch::empty({B, H, Sq, D}, q.options().dtype(out_st));
   }
   torch::Tensor lse;
   if (return_lse || lse_opt.has_value()) {
     if (lse_opt.has_value()) {
       lse = *lse_opt;
+      TORCH_CHECK(lse.device() == q.device(), "lse must be on q's device");
       TORCH_CHECK(lse.scalar_type() == at::ScalarType::Float && lse.dim() == 3 &&
                       lse.size(0) == B && lse.size(1) == H && lse.size(2) == Sq &&
                       lse.stride(2) == 1,
@@ -137,6 +143,7 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
   p.v_stride_b = vt.stride(0);
   p.v_stride_h = vt.stride(1);
   p.v_stride_r = vt.stride(2);
+  p.v_layout = v_code;
   p.o_stride_b = out.stride(0);
   p.o_stride_h = out.stride(1);
   p.o_stride_s = out.stride(2);
@@ -146,7 +153,7 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
   }
   p.softmax_scale = static_cast<float>(softmax_scale);
   p.causal = causal ? 1 : 0;
-  p.out_dtype = e4m3_out ? FA8_OUT_E4M3 : FA8_OUT_F16;
+  p.out_dtype = out_dtype == "e4m3" ? FA8_OUT_E4M3 : (out_dtype == "fp32" ? FA8_OUT_F32 : FA8_OUT_F16);
   p.q_offset = q_offset;
   p.kv_offset = kv_offset;
   p.split_keys = static_cast<int32_t>(split_keys);
@@ -201,18 +208,23 @@ std::vector<torch::Tensor> flash_attn_fp8_forward_ex(
 }
 
 // Variable-length (packed) batches: q (total_q, H, D), k (total_kv, H_kv, D),
-// v (total_kv, H_kv, D) ("thd") or pre-transposed (H_kv, D, total_kv) ("hdt");
-// cu_seqlens_* int32 (batch + 1). Returns [out (total_q, H, D)] (+ lse (H, total_q)).
+// v (total_kv, H_kv, D) ("thd", read in place as BHSD rows) or pre-transposed
+// (H_kv, D, total_kv) ("hdt"); cu_seqlens_* int32 (batch + 1) on q's device.
+// The offsets are never copied to the host: the kernel validates each
+// sequence and reports refusals in the optional int32 `status` word.
+// Returns [out (total_q, H, D)] (+ lse (H, total_q)).
 std::vector<torch::Tensor> flash_attn_fp8_varlen_forward(
     torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens_q,
     torch::Tensor cu_seqlens_kv, int64_t max_seqlen_q, bool causal,
     c10::optional<double> softmax_scale, std::string v_layout, bool return_lse,
-    std::string out_dtype) {
+    std::string out_dtype, c10::optional<torch::Tensor> status) {
   for (auto* t : {&q, &k, &v}) {
     TORCH_CHECK(t->device().is_cuda() && t->scalar_type() == at::ScalarType::Float8_e4m3fn,
                 "q, k, v must be CUDA float8_e4m3fn tensors");
     TORCH_CHECK(t->dim() == 3, "q, k, v must be 3-D (packed)");
   }
+  TORCH_CHECK(k.device() == q.device() && v.device() == q.device(),
+              "q, k, v must be on the same device");
   TORCH_CHECK(v_layout == "thd" || v_layout == "hdt", "v_layout must be 'thd' or 'hdt'");
   TORCH_CHECK(out_dtype == "fp16" || out_dtype == "e4m3", "out_dtype must be 'fp16' or 'e4m3'");
   const int64_t Tq = q.size(0), H = q.size(1), D = q.size(2);
@@ -220,41 +232,53 @@ std::vector<torch::Tensor> flash_attn_fp8_varlen_forward(
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
   TORCH_CHECK(k.size(2) == D && Hkv > 0 && H % Hkv == 0, "k must be (total_kv, H_kv, D)");
   TORCH_CHECK(cu_seqlens_q.dim() == 1 && cu_seqlens_q.numel() >= 2 &&
-                  cu_seqlens_kv.numel() == cu_seqlens_q.numel(),
+                  cu_seqlens_kv.dim() == 1 && cu_seqlens_kv.numel() == cu_seqlens_q.numel(),
               "cu_seqlens_q / cu_seqlens_kv must be 1-D with batch + 1 entries");
+  TORCH_CHECK(max_seqlen_q > 0 && max_seqlen_q <= Tq, "need 0 < max_seqlen_q <= total_q");
   const int64_t B = cu_seqlens_q.numel() - 1;
-  auto cuq_h = cu_seqlens_q.to(at::kCPU).to(at::kInt);
-  auto cuk_h = cu_seqlens_kv.to(at::kCPU).to(at::kInt);
-  const int* cq = cuq_h.data_ptr<int>();
-  const int* ck = cuk_h.data_ptr<int>();
-  TORCH_CHECK(cq[0] == 0 && ck[0] == 0 && cq[B] == Tq && ck[B] == Tk,
-              "cu_seqlens must start at 0 and end at the packed lengths");
-  for (int64_t b = 0; b < B; ++b) {
-    TORCH_CHECK(cq[b + 1] >= cq[b] && ck[b + 1] >= ck[b], "cu_seqlens must be non-decreasing");
-    TORCH_CHECK(cq[b + 1] - cq[b] <= max_seqlen_q, "a sequence is longer than max_seqlen_q");
-    TORCH_CHECK(ck[b] % 16 == 0,
-                "every cu_seqlens_kv entry must be a multiple of 16 (V^T tile alignment)");
-  }
   c10::cuda::CUDAGuard guard(q.device());
   auto stream = at::cuda::getCurrentCUDAStream(q.get_device());
-  q = q.contiguous();
-  k = k.contiguous();
-  const int64_t Tk_pad = (Tk + 15) / 16 * 16;
-  torch::Tensor vt = torch::zeros({Hkv, D, Tk_pad}, v.options());
+  // Offsets live on the device as int32; other dtypes / devices are converted
+  // with device-side (or host-to-device) copies, never device-to-host.
+  auto dev_i32 = [&](const torch::Tensor& t) {
+    TORCH_CHECK(t.device().is_cpu() || t.device() == q.device(),
+                "cu_seqlens must be on q's device (or on the host)");
+    return t.to(q.device(), at::kInt).contiguous();
+  };
+  auto cuq_d = dev_i32(cu_seqlens_q);
+  auto cuk_d = dev_i32(cu_seqlens_kv);
+  if (!tma_ok(q) || q.stride(2) != 1) q = q.contiguous();
+  if (!tma_ok(k) || k.stride(2) != 1) k = k.contiguous();
+  torch::Tensor vt;
+  int v_code;
   if (v_layout == "thd") {
     TORCH_CHECK(v.size(0) == Tk && v.size(1) == Hkv && v.size(2) == D, "v must be (total_kv, H_kv, D)");
-    vt.narrow(2, 0, Tk).copy_(v.permute({1, 2, 0}));
+    vt = tma_ok(v) && v.stride(2) == 1 ? v : v.contiguous();
+    v_code = FA8_V_BHSD;
   } else {
     TORCH_CHECK(v.size(0) == Hkv && v.size(1) == D && v.size(2) == Tk, "v must be (H_kv, D, total_kv)");
-    vt.narrow(2, 0, Tk).copy_(v);
+    vt = v;
+    if (Tk % 16 != 0 || !tma_ok(vt) || vt.stride(2) != 1) {
+      const int64_t Tk_pad = (Tk + 15) / 16 * 16;
+      auto vp = torch::empty({Hkv, D, Tk_pad}, v.options());
+      vp.narrow(2, Tk, Tk_pad - Tk).zero_();
+      vp.narrow(2, 0, Tk).copy_(v);
+      vt = vp;
+    }
+    v_code = FA8_V_BHDS;
   }
   const bool e4m3_out = out_dtype == "e4m3";
   auto out = torch::empty({Tq, H, D}, q.options().dtype(e4m3_out ? at::ScalarType::Float8_e4m3fn
                                                                     : at::ScalarType::Half));
   torch::Tensor lse;
   if (return_lse) lse = torch::empty({H, Tq}, q.options().dtype(at::ScalarType::Float));
-  auto cuq_d = cuq_h.to(q.device());
-  auto cuk_d = cuk_h.to(q.device());
+  int32_t* status_ptr = nullptr;
+  if (status.has_value()) {
+    TORCH_CHECK(status->device() == q.device() && status->scalar_type() == at::kInt &&
+                    status->numel() >= 1 && status->is_contiguous(),
+                "status must be a contiguous int32 CUDA tensor on q's device");
+    status_ptr = status->data_ptr<int32_t>();
+  }
   fa8_fwd_params p;
   fa8_fwd_params_init(&p, B, H, Hkv, Tq, Tk, D);
   p.q = q.data_ptr();
@@ -262,9 +286,15 @@ std::vector<torch::Tensor> flash_attn_fp8_varlen_forward(
   p.v = vt.data_ptr();
   p.o = out.data_ptr();
   p.lse = return_lse ? lse.data_ptr<float>() : nullptr;
-  p.q_stride_s = H * D;  p.q_stride_h = D;  p.q_stride_b = Tq * H * D;
-  p.k_stride_s = Hkv * D; p.k_stride_h = D; p.k_stride_b = Tk * Hkv * D;
-  p.v_stride_r = Tk_pad; p.v_stride_h = D * Tk_pad; p.v_stride_b = Hkv * D * Tk_pad;
+  p.status = status_ptr;
+  p.q_stride_s = q.stride(0);  p.q_stride_h = q.stride(1);  p.q_stride_b = Tq * q.stride(0);
+  p.k_stride_s = k.stride(0);  p.k_stride_h = k.stride(1);  p.k_stride_b = Tk * k.stride(0);
+  if (v_code == FA8_V_BHSD) {
+    p.v_stride_r = vt.stride(0); p.v_stride_h = vt.stride(1); p.v_stride_b = Tk * vt.stride(0);
+  } else {
+    p.v_stride_r = vt.stride(1); p.v_stride_h = vt.stride(0); p.v_stride_b = Hkv * vt.stride(0);
+  }
+  p.v_layout = v_code;
   p.o_stride_s = H * D;  p.o_stride_h = D;  p.o_stride_b = 0;
   p.lse_stride_h = Tq;   p.lse_stride_b = 0;
   p.softmax_scale = static_cast<float>(softmax_scale.has_value() ? *softmax_scale
@@ -296,8 +326,8 @@ std::vector<torch::Tensor> lse_merge(std::vector<torch::Tensor> outs,
                     outs[i].scalar_type() == o0.scalar_type() && outs[i].device() == o0.device(),
                 "all outs must be contiguous with one shape / dtype / device");
     TORCH_CHECK(lses[i].is_contiguous() && lses[i].scalar_type() == at::ScalarType::Float &&
-                    lses[i].numel() == rows,
-                "lse parts must be contiguous float32 with one entry per row");
+                    lses[i].numel() == rows && lses[i].device() == o0.device(),
+                "lse parts must be contiguous float32 on the outs' device, one entry per row");
     op.push_back(outs[i].data_ptr());
     lp.push_back(lses[i].data_ptr<float>());
   }
@@ -348,7 +378,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k"), py::arg("v"), py::arg("cu_seqlens_q"), py::arg("cu_seqlens_kv"),
         py::arg("max_seqlen_q"), py::arg("causal") = true, py::arg("softmax_scale") = py::none(),
         py::arg("v_layout") = "thd", py::arg("return_lse") = false,
-        py::arg("out_dtype") = "fp16",
+        py::arg("out_dtype") = "fp16", py::arg("status") = py::none(),
         "FP8 attention over packed variable-length sequences; returns [out] or [out, lse]");
   m.def("lse_merge", &lse_merge, "log-sum-exp merge of partial attention outputs");
   m.def("quantize_e4m3", &quantize_e4m3, py::arg("x"), py::arg("scale") = 1.0,

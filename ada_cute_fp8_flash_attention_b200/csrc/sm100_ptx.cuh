@@ -222,10 +222,20 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, int row_byt
   d |= layout << 61;
   return d;
 }
-// Instruction descriptor, kind::f8f6f4: A = B = e4m3, both K-major, D = f32.
-__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(m >> 4) << 24);
+// The same descriptor describes an MN-major operand stored as rows of
+// `row_bytes` along MN (one row per K index, 128B / 64B swizzled as TMA
+// writes them): eight K-rows form a swizzle atom and consecutive atoms along K
+// are 8 * row_bytes apart (the stride byte offset); an MN extent of one row
+// needs no leading byte offset. Successive K steps of 32 (e4m3) start 32 rows
+// further on.
+__device__ __forceinline__ uint64_t smem_desc_mnmajor(uint32_t saddr, int row_bytes) {
+  return smem_desc_kmajor(saddr, row_bytes);
+}
+// Instruction descriptor, kind::f8f6f4: A = B = e4m3, A K-major, B K-major
+// (or MN-major with b_mn_major: bit 16, "transpose B"), D = f32.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n, bool b_mn_major = false) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (b_mn_major ? (1u << 16) : 0u) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ---------------------------------------------------------------- math

@@ -3,22 +3,30 @@
 
 Workload (the headline): B=4, H=32, S=4096, D=128,
 non-causal, Q/K/V ~ N(0,1) cast to e4m3, V pre-transposed (B,H,D,S), fp16 O.
-One "step" = one forward over that batch. With N GPUs each rank runs its own
-copy of the headline batch (B=4 per GPU, global batch 4N, weak scaling):
-the (batch, head) units are sharded across ranks with no collective on the
-data path; the only communication is the timing barrier and the max-reduce
-of the elapsed time.
+One "step" = one forward over that batch.
+
+With N GPUs the SAME global batch is split across the ranks (strong scaling):
+the 128 (batch, head) units of the call are cut into N contiguous ranges
+(`sharding.shard_bh`), rank r runs its range alone, and no data crosses GPUs
+(the only communication is the timing barrier and the max-reduce of the
+elapsed time). `value` is the whole call's FLOPs over the slowest rank's time.
+The weak-scaling figure (every rank runs the whole batch) is reported beside
+it. For N >= 2 the same invocation also runs the long-context config C5
+(S = 131072, causal) context-parallel across the ranks and reports it, with
+sampled-row parity against a float64 restatement, under `c5_cp`.
 
 Arms:
   (default)          this framework: device-resident inputs (`value`) and the
                      end-to-end path through the public API with pinned host
-                     buffers and host<->device copies in the timed region (`e2e`).
+                     buffers and host<->device copies in the timed region (`e2e`),
+                     with the measured pinned-copy ceiling of this run beside it.
   --impl reference   the reference's CPU path (test.py:8-15 naive attention,
                      restated in fp32 by oracle/attention_ref.py) on this host's
                      cores, over a bounded sample of the same workload.
 
-Inputs (Q/K/V 192 MiB + O 128 MiB per GPU) exceed the 126 MB L2, so no L2
-flush is needed between timed steps.
+L2: when a rank's inputs and output fit in a few times the 126 MB L2 (C2 at
+N >= 4), a buffer larger than L2 is written between timed steps and only the
+forward launches are timed (CUDA events around each step, summed).
 """
 from __future__ import annotations
 
@@ -27,7 +35,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -50,15 +57,16 @@ CONFIGS = {
                "(BASELINE configs[4])", batch=1, heads=32, seqlen=131072, head_dim=128,
                causal=True, dist="normal", sigma=1.0),
 }
-WORKLOAD = dict(CONFIGS["c2"], seed=1234)
+WORKLOAD = dict(CONFIGS["c2"], seed=1234, key="c2")
 CP_DESC = {
     "allgather": "cp{world} zig-zag chunks, async NCCL all-gather of e4m3 K/V overlapped with "
-                 "own-chunk compute, one launch per chunk pair, LSE merge",
+                 "own-chunk compute, fp32 partial O per chunk pair, LSE merge",
     "ring": "cp{world} zig-zag chunks, NCCL point-to-point ring of e4m3 K/V overlapped with "
-            "compute, one launch per chunk pair, LSE merge",
+            "compute, fp32 partial O per chunk pair, LSE merge",
 }
 METRIC = "FP8 attn fwd TFLOPS/GPU and % of FP8 dense peak; ms/call at 1/2/4/8 B200"
 FP8_SPEC_TFLOPS = 4500.0
+L2_BYTES = 126e6
 
 
 def flops(batch, heads, sq, skv, d, causal):
@@ -78,26 +86,27 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def load_traffic():
-    """DRAM bytes per launch from the committed ncu summary (None if absent)."""
-    p = ROOT / "profiles" / "fa8_fwd_kernel_c2.md"
+def load_traffic(key, units):
+    """DRAM bytes of one launch over `units` (batch, head) units, from the ncu
+    capture of this workload recorded in profiles/dram_traffic.json, scaled by
+    units processed; None (with the reason) when no capture of it exists."""
+    p = ROOT / "profiles" / "dram_traffic.json"
     if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+        return None, "no ncu capture recorded (profiles/dram_traffic.json absent)"
+    rec = json.loads(p.read_text()).get(key)
+    if not rec:
+        return None, f"no ncu capture recorded for workload {key}"
+    per_unit = rec["dram_bytes"] / rec["units"]
+    return per_unit * units, (f"ncu dram__bytes_read+write of {rec['units']} units "
+                              f"({rec['shape']}), scaled to {units} units")
 
 
 class ClockSampler:
     """SM clock / throttle-reason sampling while the timed region runs.
 
-    Polls NVML from a background thread every ~5 ms (nvidia-smi's 100 ms
-    loop would see almost nothing of a timed region of a few tens of ms);
-    falls back to nvidia-smi when NVML is unavailable.
+    Polls NVML (pynvml) from a background thread every ~5 ms; nvidia-smi's
+    100 ms loop would see almost nothing of a timed region of tens of ms. With
+    no NVML the summary says "unsampled".
     """
 
     REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
@@ -110,6 +119,7 @@ class ClockSampler:
         self._thread = None
         self._nvml = None
         self._handle = None
+        self.max_mhz = None
 
     def _open(self):
         import pynvml
@@ -156,7 +166,7 @@ class ClockSampler:
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
         reasons = sorted({name for _, _, bits in self.rows
                           for name, bit in self.REASON_BITS.items() if bits & bit})
         return {"sm_mhz": statistics.median(r[0] for r in self.rows),
@@ -165,7 +175,7 @@ class ClockSampler:
                 "reasons": reasons, "source": "NVML, 5 ms poll during the timed region"}
 
 
-def dist_setup(args):
+def dist_setup():
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -177,22 +187,50 @@ def dist_setup(args):
     return world, rank, local
 
 
-def make_inputs_dev(device, rank):
-    """This rank's shard: B=4 (per GPU) x H x S x D, seeded per global (batch) index."""
+class Ranks:
+    """Barrier and max-over-ranks for the timing (no-ops on one GPU)."""
+
+    def __init__(self, world, device):
+        self.world, self.device = world, device
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, x):
+        if self.world == 1:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x):
+        if self.world == 1:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+
+def draw_global_inputs():
+    """The whole call's Q, K, V^T on the host, seeded once (same on every rank)."""
     import torch
 
     W = WORKLOAD
     B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
-    seed = W["seed"] + 1000 * rank
-    gen = torch.Generator(device="cpu").manual_seed(seed)
-    # Drawn on the host (the e2e arm copies them from pinned memory), cast to
-    # e4m3 with scale 1.0 (round to nearest even).
+    gen = torch.Generator(device="cpu").manual_seed(W["seed"])
+
     def draw(shape):
         if W["dist"] == "uniform":
             x = torch.rand(shape, generator=gen) * 4.0 - 2.0
         else:
             x = torch.randn(shape, generator=gen) * W["sigma"]
-        return x.to(torch.float8_e4m3fn)
+        return x.to(torch.float8_e4m3fn)  # scale 1.0, round to nearest even
 
     return draw((B, H, S, D)), draw((B, H, S, D)), draw((B, H, D, S))
 
@@ -223,13 +261,26 @@ def fp8_gemm_probe(device):
         return None
 
 
+def config_dict(world):
+    """The `config` of both arms (identical for the same workload and N)."""
+    W = WORKLOAD
+    B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
+    per_rank_bytes = algo_bytes(B, H, S, S, D) / world
+    return {"workload": W["name"], "global_batch": B, "seq_len": S, "heads": H,
+            "head_dim": D, "causal": W["causal"],
+            "parallelism": (f"{world} GPUs, (batch, head) units of one call split in "
+                            f"contiguous ranges, no collective" if world > 1 else "1 GPU"),
+            "l2": ("L2 flushed between timed steps (a rank's data fits in L2)"
+                   if per_rank_bytes < 3 * L2_BYTES
+                   else "inputs larger than L2")}
+
+
 def cpu_baseline_sample(max_seconds=12.0):
     """test.py's naive attention (fp32, CPU oracle) on a bounded sample of the workload.
 
-    Times whole (batch, head) units of the headline shape; returns TFLOPS and a
-    description. Runs with every host thread numpy's BLAS is allowed to use.
+    Times whole (batch, head) units of the workload's shape; returns TFLOPS and
+    the sample. Runs with every host thread numpy's BLAS is allowed to use.
     """
-    import numpy as np
     from oracle.attention_ref import attention, e4m3_decode, make_inputs
 
     W = WORKLOAD
@@ -255,28 +306,30 @@ def run_reference(args):
     if rank != 0:
         return 0
     W = WORKLOAD
+    B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
     cores = os.cpu_count()
     vals = []
     per_step = max(2.0, 60.0 / max(1, args.steps + args.warmup))
+    units, el = 0, 0.0
     for i in range(args.warmup + args.steps):
         tf, units, el = cpu_baseline_sample(max_seconds=per_step)
         if i >= args.warmup:
             vals.append(tf)
     v = statistics.median(vals)
-    total_flops = flops(W["batch"], W["heads"], W["seqlen"], W["seqlen"], W["head_dim"],
-                        W["causal"])
-    sample = (f"{units} of {W['batch'] * W['heads']} (batch, head) units of the workload per "
-              f"step, extrapolated by FLOPs")
+    total_flops = flops(B, H, S, S, D, W["causal"])
+    sample = (f"{units} of {B * H} (batch, head) units of the workload per step "
+              f"({el:.1f} s), extrapolated to the whole call by FLOPs")
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOPS",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": total_flops / (v * 1e12) * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": W["name"],
-                   "global_batch": W["batch"], "seq_len": W["seqlen"], "heads": W["heads"],
-                   "head_dim": W["head_dim"], "causal": W["causal"],
-                   "path": "test.py:8-15 naive attention, fp32 numpy on host cores "
-                           "(oracle/attention_ref.py)"},
+        "ms_per_step": total_flops / (v * 1e12) * 1e3, "extrapolated": True,
+        "ms_per_step_basis": "whole call extrapolated from the timed sample by FLOPs",
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": config_dict(world),
+        "path": "test.py:8-15 naive attention, fp32 numpy on the host cores "
+                "(oracle/attention_ref.py); one host serves every N",
         "cpu_baseline": {"value": v, "unit": "TFLOPS", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": v, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -285,76 +338,137 @@ def run_reference(args):
     return 0
 
 
+def time_steps(step, n, stream, flush=None):
+    """Device time (ms) of n calls of step(): one event pair around the loop, or,
+    with flush (an L2-clearing write issued before every call), per-call event
+    pairs with the flushes outside them."""
+    import torch
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n)]
+    for a, b in evs:
+        flush()
+        a.record(stream)
+        step()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def pinned_link_ceiling(device, nbytes, ranks):
+    """Pinned host<->device copy rate (GB/s per rank, both directions at once, all
+    ranks together) measured with the same byte counts as one e2e step."""
+    import torch
+    h_up = torch.empty(nbytes[0], dtype=torch.uint8).pin_memory()
+    h_dn = torch.empty(nbytes[1], dtype=torch.uint8).pin_memory()
+    d_up = torch.empty(nbytes[0], dtype=torch.uint8, device=device)
+    d_dn = torch.empty(nbytes[1], dtype=torch.uint8, device=device)
+    s_up, s_dn = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    for _ in range(2):
+        with torch.cuda.stream(s_up):
+            d_up.copy_(h_up, non_blocking=True)
+        with torch.cuda.stream(s_dn):
+            h_dn.copy_(d_dn, non_blocking=True)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    reps = 4
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record(s_up)
+    e[2].record(s_dn)
+    for _ in range(reps):
+        with torch.cuda.stream(s_up):
+            d_up.copy_(h_up, non_blocking=True)
+        with torch.cuda.stream(s_dn):
+            h_dn.copy_(d_dn, non_blocking=True)
+    e[1].record(s_up)
+    e[3].record(s_dn)
+    torch.cuda.synchronize()
+    ms_up, ms_dn = ranks.max(e[0].elapsed_time(e[1])), ranks.max(e[2].elapsed_time(e[3]))
+    return (reps * nbytes[0] / (ms_up * 1e-3) / 1e9, reps * nbytes[1] / (ms_dn * 1e-3) / 1e9)
+
+
 def run_framework(args):
     import torch
 
-    world, rank, local = dist_setup(args)
+    world, rank, local = dist_setup()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     import ada_cute_fp8_flash_attention_b200 as fa8
+    from ada_cute_fp8_flash_attention_b200 import sharding
 
+    ranks = Ranks(world, device)
     W = WORKLOAD
     B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
     causal = W["causal"]
-    q_h, k_h, v_h = make_inputs_dev(device, rank)
-    q, k, v = q_h.to(device), k_h.to(device), v_h.to(device)
-    out = torch.empty((B, H, S, D), dtype=torch.float16, device=device)
+    q_g, k_g, v_g = draw_global_inputs()
+    qs_h, ks_h, vs_h, (h0, h1) = sharding.shard_bh(q_g, k_g, v_g, rank, world)
+    U = h1 - h0
+    qs_h, ks_h, vs_h = qs_h.contiguous(), ks_h.contiguous(), vs_h.contiguous()
+    q, k, v = qs_h.to(device), ks_h.to(device), vs_h.to(device)
+    out = torch.empty((1, U, S, D), dtype=torch.float16, device=device)
     stream = torch.cuda.current_stream(device)
-
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        import torch.distributed as dist
-        t = torch.tensor([x], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    flush_buf = None
+    if algo_bytes(1, U, S, S, D) < 3 * L2_BYTES:
+        flush_buf = torch.empty(int(2 * L2_BYTES), dtype=torch.uint8, device=device)
+    flush = (lambda: flush_buf.zero_()) if flush_buf is not None else None  # noqa: E731
 
     step = lambda: fa8.flash_attn_fp8_forward_ex(q, k, v, causal=causal, out=out)  # noqa: E731
 
-    # ---- device-resident timed region
+    # ---- device-resident timed region: this rank's share of the one call
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    barrier()
+    ranks.barrier()
     torch.cuda.synchronize()
     launches0 = fa8.launch_count()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    barrier()
+        ms_local = time_steps(step, args.steps, stream, flush)
+    ranks.barrier()
     launches = fa8.launch_count() - launches0
-    ms_local = ev0.elapsed_time(ev1)
-    ms = max_over_ranks(ms_local)
+    ms = ranks.max(ms_local)
     ms_step = ms / args.steps
-    f_rank = flops(B, H, S, S, D, causal)
-    total_flops = f_rank * world
-    value = total_flops / (ms_step * 1e-3) / 1e12  # whole-job TFLOPS
-    kern_tflops = f_rank / (ms_local / args.steps * 1e-3) / 1e12  # this rank's kernel
+    total_flops = flops(B, H, S, S, D, causal)
+    value = total_flops / (ms_step * 1e-3) / 1e12  # whole-call TFLOPS over all GPUs
+    f_rank = flops(1, U, S, S, D, causal)
+    kern_ms = ms_local / args.steps
+    kern_tflops = f_rank / (kern_ms * 1e-3) / 1e12  # this rank's kernel
+
+    # ---- weak scaling (every rank runs the whole call), reported beside it
+    weak = None
+    if world > 1 and not args.no_weak:
+        qw, kw, vw = q_g.to(device), k_g.to(device), v_g.to(device)
+        ow = torch.empty((B, H, S, D), dtype=torch.float16, device=device)
+        wstep = lambda: fa8.flash_attn_fp8_forward_ex(qw, kw, vw, causal=causal, out=ow)  # noqa: E731
+        for _ in range(args.warmup):
+            wstep()
+        torch.cuda.synchronize()
+        ranks.barrier()
+        wms = ranks.max(time_steps(wstep, args.steps, stream)) / args.steps
+        weak = {"value": total_flops * world / (wms * 1e-3) / 1e12, "unit": "TFLOPS",
+                "ms_per_step": wms, "global_batch": B * world,
+                "what": "every rank runs the whole C2 call; whole-job TFLOPS"}
+        del qw, kw, vw, ow
 
     # ---- end-to-end through the public API with pinned host buffers
-    # Every step copies its Q/K/V from pinned host memory, runs the forward and
-    # copies O back to pinned host memory. Steps are pipelined over three
-    # streams (host->device, compute, device->host) with double buffers, as a
-    # serving loop would: step k's uploads overlap step k-1's compute and
+    # Every step copies this rank's Q/K/V shard from pinned host memory, runs the
+    # forward and copies O back to pinned host memory. Steps are pipelined over
+    # three streams (host->device, compute, device->host) with double buffers,
+    # as a serving loop would: step k's uploads overlap step k-1's compute and
     # step k-2's download. The timed region spans the first upload to the last
     # download.
-    qp, kp, vp = q_h.pin_memory(), k_h.pin_memory(), v_h.pin_memory()
-    ops = [torch.empty((B, H, S, D), dtype=torch.float16).pin_memory() for _ in range(2)]
-    # Enough steps that the unoverlapped first upload and last download (pipeline
-    # fill and drain) are a small part of the timed region, as in a serving loop.
+    qp, kp, vp = qs_h.pin_memory(), ks_h.pin_memory(), vs_h.pin_memory()
+    ops = [torch.empty((1, U, S, D), dtype=torch.float16).pin_memory() for _ in range(2)]
     e_steps = 0 if args.no_e2e else max(8, min(2 * args.steps, 48))
     s_up, s_comp, s_down = (torch.cuda.Stream(device) for _ in range(3))
     dbuf = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
-             torch.empty((B, H, S, D), dtype=torch.float16, device=device)) for _ in range(2)]
+             torch.empty((1, U, S, D), dtype=torch.float16, device=device)) for _ in range(2)]
     up_done = [torch.cuda.Event() for _ in range(2)]
     comp_done = [torch.cuda.Event() for _ in range(2)]
     down_done = [torch.cuda.Event() for _ in range(2)]
@@ -381,11 +495,13 @@ def run_framework(args):
                 ops[b].copy_(od, non_blocking=True)
                 down_done[b].record(s_down)
 
-    e_ms, e2e_val = None, None
+    h2d = q.numel() + k.numel() + v.numel()
+    d2h = ops[0].numel() * 2
+    e_ms, e2e_val, link = None, None, None
     if e_steps:
         e2e_run(2)
         torch.cuda.synchronize()
-        barrier()
+        ranks.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s_up)
@@ -394,14 +510,20 @@ def run_framework(args):
         s_up.wait_stream(s_comp)
         e1.record(s_up)
         torch.cuda.synchronize()
-        barrier()
-        e_ms = max_over_ranks(e0.elapsed_time(e1)) / e_steps
+        ranks.barrier()
+        e_ms = ranks.max(e0.elapsed_time(e1)) / e_steps
         e2e_val = total_flops / (e_ms * 1e-3) / 1e12
-    op = ops[0]
-    h2d = q.numel() + k.numel() + v.numel()
-    d2h = op.numel() * 2
+        up_gbs, dn_gbs = pinned_link_ceiling(device, (h2d, d2h), ranks)
+        floor_ms = max(h2d / (up_gbs * 1e9), d2h / (dn_gbs * 1e9)) * 1e3
+        floor_ms = max(floor_ms, kern_ms)
+        link = {"h2d_gbs_per_gpu": up_gbs, "d2h_gbs_per_gpu": dn_gbs,
+                "aggregate_h2d_gbs": up_gbs * world, "aggregate_d2h_gbs": dn_gbs * world,
+                "floor_ms_per_step": floor_ms,
+                "frac": floor_ms / e_ms,
+                "what": "pinned copies of one step's bytes, both directions at once on all "
+                        "ranks, measured in this run; floor = max(copy time, kernel time)"}
 
-    probe = fp8_gemm_probe(device) if rank == 0 else None
+    probe = fp8_gemm_probe(device) if rank == 0 and not args.no_probe else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tf, units, el = cpu_baseline_sample(max_seconds=args.cpu_seconds)
@@ -409,21 +531,21 @@ def run_framework(args):
                "sample": f"{units} (batch, head) units of the workload (S={S}, D={D}, "
                          f"causal={causal}) in {el:.1f}s, test.py:8-15 math in fp32 numpy"}
 
+    c5 = None
+    if world > 1 and not args.no_cp:
+        c5 = run_c5_cp(args, world, rank, local, device, ranks)
+
     if rank == 0:
         hbm, bf16, src = load_peaks()
         fp8_peak = 2.0 * bf16
-        traffic = load_traffic()
+        traffic, traffic_src = load_traffic(W["key"], U)
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "e4m3", "data": "synthetic",
-            "config": {"workload": W["name"] + ", per GPU", "global_batch": B * world,
-                       "seq_len": S,
-                       "heads": H, "head_dim": D, "causal": causal,
-                       "parallelism": f"dp{world} over (batch, head), no collective",
-                       "l2": ("inputs larger than L2" if algo_bytes(B, H, S, S, D) > 126e6
-                              else "inputs fit in L2; consecutive steps reuse them")},
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
+            "config": config_dict(world),
+            "units_per_gpu": U,
             "tflops_per_gpu": value / world,
             "pct_fp8_spec_peak": 100.0 * value / world / FP8_SPEC_TFLOPS,
             "pct_fp8_2x_measured_bf16": 100.0 * value / world / fp8_peak,
@@ -431,19 +553,24 @@ def run_framework(args):
             "roofline": {"bound": "tensor", "achieved": kern_tflops, "peak": fp8_peak,
                          "unit": "TFLOP/s", "frac": kern_tflops / fp8_peak,
                          "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src}); "
-                                        "FP8 tensor rate is twice bf16",
+                                        "the FP8 tensor rate is twice bf16 (of measured)",
                          "frac_of_spec_4500": kern_tflops / FP8_SPEC_TFLOPS,
                          "frac_of_fp8_gemm_probe": (kern_tflops / probe) if probe else None,
                          "algorithmic_flops_per_launch": f_rank,
-                         "hbm_gbs": algo_bytes(B, H, S, S, D) / (ms_local / args.steps * 1e-3) / 1e9,
-                         "traffic": traffic},
+                         "kernel_ms": kern_ms,
+                         "hbm_gbs": algo_bytes(1, U, S, S, D) / (kern_ms * 1e-3) / 1e9,
+                         "hbm_frac": algo_bytes(1, U, S, S, D) / (kern_ms * 1e-3) / 1e9 / hbm,
+                         "traffic": traffic, "traffic_source": traffic_src},
+            "weak_scaling": weak,
             "e2e": {"value": e2e_val, "unit": "TFLOPS", "ms_per_step": e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "link": link,
                     "path": "flash_attn_fp8_forward_ex with pinned host Q/K/V and O, "
                             "upload / compute / download pipelined on three streams"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "c5_cp": c5,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -452,70 +579,143 @@ def run_framework(args):
     return 0
 
 
-def run_context_parallel(args):
-    """C5: one causal sequence of 131072 tokens split over all ranks (zig-zag ring)."""
+def c5_chunk(cid, salt, shape, device, seed):
+    """One zig-zag chunk of the C5 inputs, drawn on the device (seeded per chunk)."""
     import torch
+    g = torch.Generator(device=device).manual_seed(seed + 7919 * cid + salt)
+    return torch.randn(shape, generator=g, device=device).to(torch.float8_e4m3fn)
 
-    world, rank, local = dist_setup(args)
-    device = torch.device("cuda", local)
+
+def run_c5_cp(args, world, rank, local, device, ranks):
+    """C5 (one causal sequence of 131072 tokens) context-parallel over the ranks,
+    timed, with sampled query rows checked against a float64 restatement of the
+    attention math on the host and the rate of the same call on one GPU."""
+    import numpy as np
+    import torch
     import torch.distributed as dist
     import ada_cute_fp8_flash_attention_b200 as fa8
     from ada_cute_fp8_flash_attention_b200 import context_parallel as cp
 
-    W = WORKLOAD
-    B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
+    C = CONFIGS["c5"]
+    B, H, S, D = C["batch"], C["heads"], C["seqlen"], C["head_dim"]
+    seed = 4321
     zz = cp.ZigZag(world, S)
     c = zz.chunk
-    gen = torch.Generator(device="cpu").manual_seed(W["seed"])
-    # Each rank draws only its own chunks (seeded per chunk id).
-    def chunk(shape_fn, salt):
-        parts = []
-        for cid in zz.chunks_of(rank):
-            g = torch.Generator(device="cpu").manual_seed(W["seed"] + 7919 * cid + salt)
-            parts.append((torch.randn(shape_fn(), generator=g) * W["sigma"]).to(torch.float8_e4m3fn))
-        return parts
-    ql = torch.cat(chunk(lambda: (B, H, c, D), 1), dim=2).to(device)
-    kl = torch.cat(chunk(lambda: (B, H, c, D), 2), dim=2).to(device)
-    vl = torch.cat(chunk(lambda: (B, H, D, c), 3), dim=3).to(device)
-    del gen
+    mine = zz.chunks_of(rank)
+    ql = torch.cat([c5_chunk(i, 1, (B, H, c, D), device, seed) for i in mine], dim=2)
+    kl = torch.cat([c5_chunk(i, 2, (B, H, c, D), device, seed) for i in mine], dim=2)
+    vl = torch.cat([c5_chunk(i, 3, (B, H, D, c), device, seed) for i in mine], dim=3)
     step = lambda: cp.ring_attention(ql, kl, vl, zz, rank, schedule=args.cp_schedule)  # noqa: E731
-    for _ in range(args.warmup):
-        step()
+    for _ in range(2):
+        o_loc, l_loc = step()
     torch.cuda.synchronize()
-    dist.barrier() if world > 1 else None
-    launches0 = fa8.launch_count()
+    ranks.barrier()
+    n = args.cp_steps
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record()
-        for _ in range(args.steps):
-            step()
-        e1.record()
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    e0.record()
+    for _ in range(n):
+        o_loc, l_loc = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = ranks.max(e0.elapsed_time(e1) / n)
     total = flops(B, H, S, S, D, True)
-    value = total / (ms * 1e-3) / 1e12
+
+    # The same call on one GPU (rank 0 alone; the others wait at the barrier).
+    one_ms = None
+    o_one = None
     if rank == 0:
-        hbm, bf16, src = load_peaks()
-        line = {"metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        chunks = range(2 * world)
+        qf = torch.cat([c5_chunk(i, 1, (B, H, c, D), device, seed) for i in chunks], dim=2)
+        kf = torch.cat([c5_chunk(i, 2, (B, H, c, D), device, seed) for i in chunks], dim=2)
+        vf = torch.cat([c5_chunk(i, 3, (B, H, D, c), device, seed) for i in chunks], dim=3)
+        o1 = fa8.flash_attn_fp8_forward_ex(qf, kf, vf, causal=True)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(2):
+            o1 = fa8.flash_attn_fp8_forward_ex(qf, kf, vf, causal=True)
+        b.record()
+        torch.cuda.synchronize()
+        one_ms = a.elapsed_time(b) / 2
+        o_one = o1
+    ranks.barrier()
+
+    # Sampled rows: first / last row of every chunk plus fixed random rows, two heads.
+    rng = np.random.default_rng(7)
+    rows = sorted(set([0, S - 1] + [j * c for j in range(2 * world)] +
+                      [j * c - 1 for j in range(1, 2 * world)] +
+                      rng.integers(0, S, 12).tolist()))
+    heads = [0, H - 1]
+    # this rank's outputs for the sampled rows it owns (global row -> local index)
+    local_rows = {}
+    for slot, cid in enumerate(mine):
+        for r in rows:
+            if cid * c <= r < (cid + 1) * c:
+                local_rows[r] = slot * c + (r - cid * c)
+    got = {(h, r): o_loc[0, h, li].float().cpu().numpy() for h in heads
+           for r, li in local_rows.items()}
+    parts = [None] * world
+    dist.all_gather_object(parts, got)
+    res = None
+    if rank == 0:
+        merged = {}
+        for p_ in parts:
+            merged.update(p_)
+        qh = qf[0, heads].float().cpu().numpy().astype(np.float64)
+        kh = kf[0, heads].float().cpu().numpy().astype(np.float64)
+        vh = vf[0, heads].float().cpu().numpy().astype(np.float64)  # (2, D, S)
+        errs, errs_one = [], []
+        for hi, h in enumerate(heads):
+            for r in rows:
+                s_ = kh[hi, :r + 1] @ qh[hi, r] / math.sqrt(D)
+                p_ = np.exp(s_ - s_.max())
+                ref_row = (vh[hi, :, :r + 1] @ p_) / p_.sum()
+                errs.append(np.abs(merged[(h, r)] - ref_row))
+                errs_one.append(np.abs(o_one[0, h, r].float().cpu().numpy() - ref_row))
+        errs, errs_one = np.concatenate(errs), np.concatenate(errs_one)
+        res = {"workload": C["name"], "n_gpus": world, "ms_per_step": ms,
+               "value": total / (ms * 1e-3) / 1e12, "unit": "TFLOPS",
+               "tflops_per_gpu": total / (ms * 1e-3) / 1e12 / world,
+               "one_gpu_ms": one_ms, "one_gpu_tflops": total / (one_ms * 1e-3) / 1e12,
+               "efficiency_vs_one_gpu": (one_ms / ms) / world,
+               "schedule": CP_DESC[args.cp_schedule].format(world=world),
+               "steps": n,
+               "parity": {"rows": len(rows), "heads": heads,
+                          "max_err": float(errs.max()), "mean_err": float(errs.mean()),
+                          "one_gpu_max_err": float(errs_one.max()),
+                          "one_gpu_mean_err": float(errs_one.mean()),
+                          "tolerance": {"max": 2e-2, "mean": 2e-3},
+                          "reference": "float64 softmax(q k^T / sqrt(D)) v on the host, "
+                                       "causal, same e4m3 inputs"}}
+        del qf, kf, vf, o_one
+    ranks.barrier()
+    return res
+
+
+def run_context_parallel_line(args):
+    """--workload c5: the context-parallel C5 line alone (N >= 1)."""
+    import torch
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    ranks = Ranks(world, device)
+    with ClockSampler(local) as clk:
+        res = run_c5_cp(args, world, rank, local, device, ranks)
+    if rank == 0:
+        C = CONFIGS["c5"]
+        line = {"metric": METRIC, "value": res["value"], "unit": "TFLOPS", "n_gpus": world,
+                "steps": res["steps"], "warmup": 2, "ms_per_step": res["ms_per_step"],
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "e4m3", "data": "synthetic",
-                "config": {"workload": W["name"], "global_batch": B, "seq_len": S,
-                           "heads": H, "head_dim": D, "causal": True,
-                           "parallelism": CP_DESC[args.cp_schedule].format(world=world)},
-                "tflops_per_gpu": value / world,
-                "pct_fp8_spec_peak": 100.0 * value / world / FP8_SPEC_TFLOPS,
-                "pct_fp8_2x_measured_bf16": 100.0 * value / world / (2 * bf16),
-                "gpu_launches": fa8.launch_count() - launches0,
-                "clocks": clk.summary()}
+                "config": {"workload": C["name"], "global_batch": C["batch"],
+                           "seq_len": C["seqlen"], "heads": C["heads"],
+                           "head_dim": C["head_dim"], "causal": True,
+                           "parallelism": res["schedule"]},
+                "c5_cp": res, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:
+        import torch.distributed as dist
         dist.destroy_process_group()
     return 0
 
@@ -529,23 +729,28 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e arm")
+    ap.add_argument("--no-weak", action="store_true", help="skip the weak-scaling figure")
+    ap.add_argument("--no-cp", action="store_true", help="skip the C5 context-parallel sub-line")
+    ap.add_argument("--no-probe", action="store_true", help="skip the cuBLASLt FP8 GEMM probe")
+    ap.add_argument("--cp-steps", type=int, default=4)
     ap.add_argument("--workload", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--cp-schedule", default="allgather", choices=["allgather", "ring"],
                     help="K/V exchange of the context-parallel workload (c5)")
     ap.add_argument("--shape", default=None,
                     help="B,H,S,D,causal override for profiling runs (not a bench line)")
     args = ap.parse_args()
-    WORKLOAD.update(CONFIGS[args.workload])
+    WORKLOAD.update(CONFIGS[args.workload], key=args.workload)
     if args.shape:
         b, h, s, d, c = args.shape.split(",")
         WORKLOAD.update(batch=int(b), heads=int(h), seqlen=int(s), head_dim=int(d),
-                        causal=c.lower() in ("1", "true", "causal", "c"))
+                        causal=c.lower() in ("1", "true", "causal", "c"),
+                        key=f"shape:{args.shape}")
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "c5":
-        return run_context_parallel(args)
+        return run_context_parallel_line(args)
     return run_framework(args)
 
 

@@ -43,17 +43,25 @@ typedef enum fa8_status {
 enum { FA8_V_BHDS = 0, FA8_V_BHSD = 1 };
 
 /* Output element type. fp16 is the north-star contract; e4m3 reproduces the
- * reference's `empty_like(q)` output (csrc/flash_attention.cu:526). */
-enum { FA8_OUT_F16 = 0, FA8_OUT_E4M3 = 1 };
+ * reference's `empty_like(q)` output (csrc/flash_attention.cu:526); fp32
+ * keeps partial outputs unrounded for a later log-sum-exp merge (context
+ * parallel). */
+enum { FA8_OUT_F16 = 0, FA8_OUT_E4M3 = 1, FA8_OUT_F32 = 2 };
 
-/* Bits the kernel ORs into *status when a bounded wait gives up. */
-enum { FA8_DEVERR_TIMEOUT = 1, FA8_DEVERR_VARLEN_ALIGN = 2 };
+/* Bits the kernel ORs into *status (an optional device word) instead of
+ * faulting or hanging: a bounded wait gave up (TIMEOUT), a varlen sequence
+ * whose K/V start is not a multiple of 16 (VARLEN_ALIGN), or a varlen
+ * sequence whose offsets leave the packed tensors or that is longer than
+ * max_seqlen_q (VARLEN_RANGE). A refused sequence is left unwritten. */
+enum { FA8_DEVERR_TIMEOUT = 1, FA8_DEVERR_VARLEN_ALIGN = 2, FA8_DEVERR_VARLEN_RANGE = 4 };
 
 /*
  * All strides are in ELEMENTS. Tensors are indexed [b][h][s][d] for Q, K and
- * O, [b][h][d][s] for V in FA8_V_BHDS layout. The innermost dimension (d for
- * Q/K/O, s for V-BHDS) must have unit stride. Q/K/V are e4m3 (1 byte),
- * O is fp16 or e4m3, LSE is fp32 [b][h][s] (natural log), optional.
+ * O, [b][h][d][s] for V in FA8_V_BHDS layout (the reference's pre-transposed
+ * V) and [b][h][s][d] in FA8_V_BHSD layout (read in place: the PV product
+ * takes the V tile as an MN-major operand). The innermost dimension (d for
+ * Q/K/O/V-BHSD, s for V-BHDS) must have unit stride. Q/K/V are e4m3 (1 byte),
+ * O is fp16, e4m3 or fp32, LSE is fp32 [b][h][s] (natural log), optional.
  */
 typedef struct fa8_fwd_params {
   const void* q;
@@ -78,8 +86,8 @@ typedef struct fa8_fwd_params {
 
   float softmax_scale;      /* natural-log scale, usually 1/sqrt(head_dim)  */
   int32_t causal;           /* mask key_pos > query_pos                     */
-  int32_t v_layout;         /* FA8_V_BHDS                                   */
-  int32_t out_dtype;        /* FA8_OUT_F16 or FA8_OUT_E4M3                  */
+  int32_t v_layout;         /* FA8_V_BHDS or FA8_V_BHSD                     */
+  int32_t out_dtype;        /* FA8_OUT_F16, FA8_OUT_E4M3 or FA8_OUT_F32     */
 
   /* Global positions of row 0 of this Q block and of this K/V block. Only
    * the causal mask reads them (context-parallel chunks); 0 otherwise. */
@@ -91,7 +99,7 @@ typedef struct fa8_fwd_params {
    * (1024), 0 disables the split. */
   int32_t split_keys;
   /* Reserved (set to 0). */
-  int32_t max_ctas;
+  int32_t reserved2;
 
   /* Per-tensor dequantisation factors of e4m3 Q, K, V (real value = code x
    * factor); 1.0 = unscaled inputs. The kernel folds descale_q * descale_k
@@ -108,8 +116,11 @@ typedef struct fa8_fwd_params {
    * occupies rows cu_seqlens_q[b] .. cu_seqlens_q[b+1]-1 (device int32
    * prefix sums with batch + 1 entries, same for cu_seqlens_kv). LSE is
    * [heads][total_q]. Every cu_seqlens_kv[b] must be a multiple of 16 (V^T
-   * tiles start on 16-byte boundaries); a sequence that violates it is left
-   * unwritten and bit 2 is ORed into *status. max_seqlen_q bounds the grid. */
+   * tiles start on 16-byte boundaries). The offsets are read only on the
+   * device (no host copy, no synchronisation): a sequence that breaks the
+   * alignment rule, leaves the packed tensors or is longer than max_seqlen_q
+   * (which sizes the grid) is left unwritten and FA8_DEVERR_VARLEN_ALIGN /
+   * FA8_DEVERR_VARLEN_RANGE is ORed into *status. */
   const int32_t* cu_seqlens_q;
   const int32_t* cu_seqlens_kv;
   int64_t max_seqlen_q;
@@ -156,7 +167,8 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream);
  * lse_parts: n_parts pointers to fp32 [rows]. Parts with lse = -inf are
  * ignored. Writes o_out (fp16 [rows][head_dim], row stride o_out_stride) and
  * lse_out (fp32, may be NULL). All pointers are device pointers; the two
- * pointer arrays are host arrays of at most 16 entries.
+ * pointer arrays are host arrays of at most 16 entries. o_parts[i] and o_out
+ * must be 16-byte aligned (FA8_ERR_ALIGNMENT otherwise).
  */
 int fa8_lse_merge(int n_parts, const void* const* o_parts, int o_is_f16,
                   const float* const* lse_parts, int64_t rows,
@@ -164,11 +176,15 @@ int fa8_lse_merge(int n_parts, const void* const* o_parts, int o_is_f16,
                   float* lse_out, void* stream);
 
 /*
- * Quantise fp16 or bf16 x[rows][cols] (row stride in elements) to e4m3 with
- * round-to-nearest-even and saturation to +-448, multiplying by `scale`
- * first. If `transpose` is set, y is written as [cols][rows] per matrix of
- * `rows` rows (batch = number of matrices, each rows x cols) — the V
- * transpose to BHDS. in_dtype: 0 = fp16, 1 = bf16.
+ * Quantise fp16 or bf16 x to e4m3 with round-to-nearest-even and saturation
+ * to +-448, multiplying by `scale` first. x holds `batch` contiguous matrices
+ * of rows x cols elements each (no row padding; the row stride is cols). If
+ * `transpose` is set, y is written as batch contiguous matrices of cols x rows
+ * — the V transpose to BHDS — else y has x's layout. in_dtype: 0 = fp16,
+ * 1 = bf16. Without transpose the element count must be a multiple of 16 and
+ * both buffers 16-byte aligned; with transpose, rows % 16 == 0, cols % 8 == 0
+ * and 16-byte aligned buffers take the vectorised kernel, other shapes a
+ * slower per-element one.
  */
 int fa8_quantize_e4m3(const void* x, int in_dtype, void* y, int64_t batch,
                       int64_t rows, int64_t cols, float scale, int transpose,

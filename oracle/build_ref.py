@@ -13,11 +13,12 @@ Do not run the result on a GPU. On B200 it faulted with an illegal memory
 access on a repeat call at test.py's shape: for the first query block it
 prefetches K/V tile -1 (csrc/flash_attention.cu:260-268), reading 64 rows
 before the first (batch, head)'s K and V^T, which faults whenever nothing is
-mapped in front of the allocation. It is built (and importable with load())
-only as a record of the reference's code path; no test, bench leg or product
-code calls it. Outputs go to oracle/_ref/ (git-ignored).
+mapped in front of the allocation. It is built only as a record of the reference's code path; nothing in this repository
+imports or runs it, and no loader for it is provided. Outputs go to
+oracle/_ref/ (git-ignored).
 
-Usage: python oracle/build_ref.py [/path/to/reference]
+Usage: python oracle/build_ref.py /path/to/reference
+   or: FA8_REFERENCE_ROOT=/path/to/reference python oracle/build_ref.py
 """
 from __future__ import annotations
 
@@ -32,7 +33,7 @@ OUT = HERE / "_ref"
 MODULE = "ada_cute_fp8_flash_attention"
 
 
-def build(ref_root: str = "/root/reference", verbose: bool = False) -> Path:
+def build(ref_root: str, verbose: bool = False) -> Path:
     import torch
     import torch.utils.cpp_extension as ce
 
@@ -86,21 +87,8 @@ def build(ref_root: str = "/root/reference", verbose: bool = False) -> Path:
     return target
 
 
-def load():
-    """Import the prebuilt reference module from oracle/_ref (None if not built)."""
-    import importlib.util
-
-    suffix = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
-    path = OUT / f"{MODULE}{suffix}"
-    if not path.exists():
-        return None
-    import torch  # noqa: F401
-
-    spec = importlib.util.spec_from_file_location(MODULE, str(path))
-    mod = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(mod)
-    return mod
-
-
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", verbose=True))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FA8_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: build_ref.py REFERENCE_ROOT (or set FA8_REFERENCE_ROOT)")
+    print(build(root, verbose=True))

@@ -11,7 +11,8 @@ scale) are saved to
 ``tests/golden/naive_attention_cases.npz``.
 
 The generated file is committed; this script needs the reference checkout
-and is not run by the tests. Usage: python tests/golden/make_golden.py [ref_root]
+and is not run by the tests. Usage: python tests/golden/make_golden.py REFERENCE_ROOT
+(or set FA8_REFERENCE_ROOT).
 """
 from __future__ import annotations
 
@@ -37,7 +38,7 @@ def load_naive(ref_root: str):
     return ns["naive_self_attention"]
 
 
-def main(ref_root="/root/reference"):
+def main(ref_root):
     naive = load_naive(ref_root)
     g = torch.Generator().manual_seed(42)
     cases = {}
@@ -66,4 +67,8 @@ def main(ref_root="/root/reference"):
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:])
+    import os
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FA8_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (or set FA8_REFERENCE_ROOT)")
+    main(root)

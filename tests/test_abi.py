@@ -59,7 +59,8 @@ def test_params_init_defaults(abi):
 @pytest.mark.parametrize("mutate,status", [
     (lambda p: setattr(p, "head_dim", 96), "FA8_ERR_UNSUPPORTED"),
     (lambda p: setattr(p, "batch", -1), "FA8_ERR_INVALID_ARG"),
-    (lambda p: setattr(p, "v_layout", 1), "FA8_ERR_UNSUPPORTED"),
+    (lambda p: setattr(p, "v_layout", 7), "FA8_ERR_INVALID_ARG"),
+    (lambda p: (setattr(p, "v_layout", 1), setattr(p, "v_stride_r", 64)), "FA8_ERR_INVALID_ARG"),
     (lambda p: setattr(p, "heads_kv", 3), "FA8_ERR_UNSUPPORTED"),
     (lambda p: setattr(p, "q", None), "FA8_ERR_INVALID_ARG"),
     (lambda p: setattr(p, "q", 0x1008), "FA8_ERR_ALIGNMENT"),
@@ -90,5 +91,8 @@ def test_no_gpu_reports_error_not_crash(abi):
 
 def test_aux_entry_points_validate(abi):
     assert abi.lse_merge([], 1, [], 10, 128, 0x1000, 128, None) == abi.FA8_ERR_INVALID_ARG
+    # o_parts / o_out are accessed as 16-byte vectors: misaligned pointers are refused
+    assert abi.lse_merge([0x1008], 1, [0x2000], 10, 128, 0x1000, 128, None) == abi.FA8_ERR_ALIGNMENT
+    assert abi.lse_merge([0x1000], 1, [0x2000], 10, 128, 0x1008, 128, None) == abi.FA8_ERR_ALIGNMENT
     assert abi.quantize_e4m3(None, 0, 0x1000, 1, 1, 16, 1.0, 0) == abi.FA8_ERR_INVALID_ARG
     assert abi.lib().fa8_status_string(3) == b"alignment / stride requirement violated"

@@ -99,3 +99,50 @@ def test_zigzag_bookkeeping():
     assert [zz.source_rank(3, s) for s in range(8)] == [3, 2, 1, 0, 7, 6, 5, 4]
     with pytest.raises(ValueError):
         _ = cp.ZigZag(3, 100).chunk
+
+
+def _stall_worker(rank, world, port, out_q, schedule, stop_evt):
+    """Step 1: every rank takes part. Step 2: rank 1 stops sending (it never
+    enters the exchange); rank 0 must raise CPTimeoutError within its deadline."""
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    S, B, H, D = 64 * 2 * world, 1, 2, 64
+    q = torch.from_numpy(ref.make_inputs((B, H, S, D), "normal", 1)).view(torch.float8_e4m3fn)
+    k = torch.from_numpy(ref.make_inputs((B, H, S, D), "normal", 2)).view(torch.float8_e4m3fn)
+    v = torch.from_numpy(ref.make_inputs((B, H, D, S), "normal", 3)).view(torch.float8_e4m3fn)
+    zz = cp.ZigZag(world, S)
+    args = (cp.split_local(q, zz, rank, 2), cp.split_local(k, zz, rank, 2),
+            cp.split_local(v, zz, rank, 3), zz, rank)
+    cp.ring_attention(*args, compute=cpu_compute, merge=cpu_merge, schedule=schedule,
+                      deadline_s=30.0)
+    dist.barrier()
+    if rank == 1:
+        stop_evt.wait(60)  # stays alive but sends nothing, until rank 0 has reported
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        cp.ring_attention(*args, compute=cpu_compute, merge=cpu_merge, schedule=schedule,
+                          deadline_s=2.0)
+        out_q.put(("no error", time.monotonic() - t0))
+    except cp.CPTimeoutError as e:
+        out_q.put(("timeout", time.monotonic() - t0, str(e)))
+    stop_evt.set()
+    os._exit(0)  # pending gloo work of the abandoned step: no orderly teardown
+
+
+@pytest.mark.parametrize("schedule", ["ring", "allgather"])
+def test_rank_that_stops_sending_is_detected_within_the_deadline(schedule):
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    stop = ctx.Event()
+    port = _free_port()
+    procs = [ctx.Process(target=_stall_worker, args=(r, 2, port, q_out, schedule, stop))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    res = q_out.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == "timeout", res
+    assert 2.0 <= res[1] < 10.0, res

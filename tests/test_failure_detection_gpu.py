@@ -78,3 +78,32 @@ def test_varlen_misaligned_kv_start_is_refused_in_kernel(abi, cuda):
     o = out.float().cpu().numpy()
     assert np.all(o[10:] == 7.0), "the refused sequence must be left unwritten"
     assert np.all(o[:10] == 0.0)
+
+
+def test_varlen_out_of_range_sequence_is_refused_in_kernel(abi, cuda):
+    """Offsets past the packed tensors (or a sequence longer than max_seqlen_q) set
+    bit 4 and leave the sequence unwritten instead of storing out of bounds."""
+    import torch
+    q = torch.zeros((48, 2, 64), dtype=torch.float8_e4m3fn, device=cuda)
+    k = torch.zeros((48, 2, 64), dtype=torch.float8_e4m3fn, device=cuda)
+    vt = torch.zeros((2, 64, 48), dtype=torch.float8_e4m3fn, device=cuda)
+    out = torch.full((48, 2, 64), 7.0, dtype=torch.float16, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    # sequence 0: rows 0..15 (fine); sequence 1: claims rows 16..79 of 48
+    cuq = torch.tensor([0, 16, 80], dtype=torch.int32, device=cuda)
+    cuk = torch.tensor([0, 16, 32], dtype=torch.int32, device=cuda)
+    p = abi.params(2, 2, 2, 48, 48, 64)
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), vt.data_ptr(), out.data_ptr()
+    p.q_stride_s, p.q_stride_h, p.q_stride_b = 128, 64, 48 * 128
+    p.k_stride_s, p.k_stride_h, p.k_stride_b = 128, 64, 48 * 128
+    p.v_stride_r, p.v_stride_h, p.v_stride_b = 48, 64 * 48, 2 * 64 * 48
+    p.o_stride_s, p.o_stride_h, p.o_stride_b = 128, 64, 0
+    p.cu_seqlens_q, p.cu_seqlens_kv = cuq.data_ptr(), cuk.data_ptr()
+    p.max_seqlen_q = 48
+    p.status = status.data_ptr()
+    abi.check(abi.fwd(p, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert int(status.item()) & 4
+    o = out.float().cpu().numpy()
+    assert np.all(o[16:] == 7.0), "the refused sequence must be left unwritten"
+    assert np.all(o[:16] == 0.0)

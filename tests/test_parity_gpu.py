@@ -96,12 +96,36 @@ def test_explicit_scale_and_e4m3_out(fa8, cuda):
     assert np.abs(got - o_q).max() <= 0.0625 * np.abs(o_ref).max() + U.MAX_ABS
 
 
-def test_bhsd_v_layout(fa8, cuda):
-    q, k, v = U.inputs(1, 2, 2, 256, 384, 64, "normal", seed=9)
+BHSD_CASES = [
+    # B, H, Hkv, Sq, Skv, D, causal
+    (1, 2, 2, 256, 384, 64, False),
+    (1, 2, 2, 256, 384, 128, False),
+    (1, 2, 2, 512, 512, 128, True),     # causal: short-prefix tiles use the hi/lo split
+    (1, 2, 2, 512, 512, 64, True),
+    (1, 2, 2, 200, 203, 128, False),    # S_kv % 16 != 0: no padding copy needed for BHSD
+    (2, 4, 2, 300, 300, 64, True),      # GQA, ragged causal
+]
+
+
+@pytest.mark.parametrize("case", BHSD_CASES, ids=lambda c: "B{}H{}x{}Sq{}Skv{}D{}{}".format(
+    c[0], c[1], c[2], c[3], c[4], c[5], "c" if c[6] else "n"))
+def test_bhsd_v_layout(fa8, cuda, case):
+    """V as (B, H_kv, S, D), read in place by the PV product (MN-major operand)."""
+    B, H, Hkv, Sq, Skv, D, causal = case
+    q, k, v = U.inputs(B, H, Hkv, Sq, Skv, D, "normal", seed=9 + Skv + D)
     v_bhsd = np.ascontiguousarray(np.swapaxes(v, 2, 3))
-    out = run_ex(fa8, q, k, v_bhsd, cuda, causal=False, v_layout="bhsd")
-    o_ref, _ = U.oracle(q, k, v, causal=False)
+    out = run_ex(fa8, q, k, v_bhsd, cuda, causal=causal, v_layout="bhsd")
+    o_ref, _ = U.oracle(q, k, v, causal=causal)
     U.assert_close(out.float().cpu().numpy(), o_ref)
+
+
+def test_bhsd_and_bhds_agree_bitwise(fa8, cuda):
+    """Both V layouts feed the same products: identical outputs."""
+    q, k, v = U.inputs(2, 4, 4, 1024, 1024, 128, "normal", seed=31)
+    v_bhsd = np.ascontiguousarray(np.swapaxes(v, 2, 3))
+    a = run_ex(fa8, q, k, v, cuda, causal=False)
+    b = run_ex(fa8, q, k, v_bhsd, cuda, causal=False, v_layout="bhsd")
+    assert (a.float() == b.float()).all()
 
 
 @pytest.mark.parametrize("q_off,kv_off", [(512, 0), (0, 512), (256, 128), (1024, 512)])
@@ -235,9 +259,32 @@ def test_varlen_packed_sequences(fa8, cuda, causal, D):
 
 
 def test_varlen_rejects_unaligned_kv_starts(fa8, cuda):
+    """The offsets are checked on the device: the bad sequence is refused, bit 2 set."""
     import torch
     q = torch.zeros((30, 2, 64), dtype=torch.float8_e4m3fn, device=cuda)
     k = torch.zeros((30, 2, 64), dtype=torch.float8_e4m3fn, device=cuda)
-    cu = torch.tensor([0, 10, 30], dtype=torch.int32)
-    with pytest.raises(RuntimeError, match="multiple of 16"):
-        fa8.flash_attn_fp8_varlen_forward(q, k, k, cu, cu, 20)
+    cu = torch.tensor([0, 10, 30], dtype=torch.int32, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    fa8.flash_attn_fp8_varlen_forward(q, k, k, cu, cu, 20, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 2
+
+
+def test_varlen_needs_no_host_sync(fa8, cuda):
+    """The varlen entry point never copies cu_seqlens to the host (no device sync)."""
+    import torch
+    lens = [128, 48, 200]
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), device=cuda)
+    T = int(sum(lens))
+    q = torch.randn((T, 4, 128), device=cuda).to(torch.float8_e4m3fn)
+    k = torch.randn((T + 16, 2, 128), device=cuda).to(torch.float8_e4m3fn)
+    cuk = torch.tensor([0, 128, 176, 384], dtype=torch.int32, device=cuda)
+    torch.cuda.synchronize()
+    prev = torch.cuda.get_sync_debug_mode()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        out = fa8.flash_attn_fp8_varlen_forward(q, k, k, cu, cuk, max(lens), causal=False)
+    finally:
+        torch.cuda.set_sync_debug_mode(prev)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
