@@ -27,6 +27,7 @@ FA8_OUT_E4M3 = 1
 EXPORTED = [
     "fa8_fwd_params_init",
     "fa8_fwd",
+    "fa8_fwd_workspace_size",
     "fa8_lse_merge",
     "fa8_quantize_e4m3",
     "fa8_status_string",
@@ -59,6 +60,8 @@ class Fa8FwdParams(C.Structure):
         ("descale_q_bh", C.c_void_p), ("descale_k_bh", C.c_void_p), ("descale_v_bh", C.c_void_p),
         ("descale_q_stride_b", C.c_int64), ("descale_q_stride_h", C.c_int64),
         ("descale_kv_stride_b", C.c_int64), ("descale_kv_stride_h", C.c_int64),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64), ("kv_splits", C.c_int32),
+        ("reserved3", C.c_int32),
     ]
 
 
@@ -75,6 +78,8 @@ def lib(path: Path | None = None) -> C.CDLL:
         L.fa8_fwd_params_init.restype = None
         L.fa8_fwd.argtypes = [C.POINTER(Fa8FwdParams), C.c_void_p]
         L.fa8_fwd.restype = C.c_int
+        L.fa8_fwd_workspace_size.argtypes = [C.POINTER(Fa8FwdParams)]
+        L.fa8_fwd_workspace_size.restype = C.c_int64
         L.fa8_lse_merge.argtypes = [C.c_int, C.POINTER(C.c_void_p), C.c_int,
                                     C.POINTER(C.c_void_p), C.c_int64, C.c_int64, C.c_void_p,
                                     C.c_int64, C.c_void_p, C.c_void_p]
@@ -109,6 +114,11 @@ def check(status: int) -> None:
 
 def fwd(p: Fa8FwdParams, stream: int = 0) -> int:
     return lib().fa8_fwd(C.byref(p), C.c_void_p(stream))
+
+
+def workspace_size(p: Fa8FwdParams) -> int:
+    """Split-KV workspace bytes fa8_fwd would use for these parameters (0: no split)."""
+    return int(lib().fa8_fwd_workspace_size(C.byref(p)))
 
 
 def lse_merge(o_ptrs, o_is_f16, lse_ptrs, rows, head_dim, o_out, o_out_stride, lse_out,

@@ -20,6 +20,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/fa8.h"
@@ -91,8 +92,49 @@ int setup_kernel_attr(int dev) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Split-KV plan of a call: shares per query tile and the workspace layout
+// [counters (qtiles x 4 B, padded to 256 B) | part_lse | part_o].
+struct SplitPlan {
+  int splits = 1;
+  int64_t qtiles = 0, cnt_bytes = 0, lse_bytes = 0, o_bytes = 0;
+  int64_t bytes() const { return splits > 1 ? cnt_bytes + lse_bytes + o_bytes : 0; }
+};
+constexpr int kSmCount = 148;
+constexpr int kMaxSplits = fa8::kMaxKvSplits;
+constexpr int64_t kMinTilesPerSplit = 8;
+
+SplitPlan plan_splits(const fa8_fwd_params* p, int splits_req) {
+  SplitPlan sp;
+  if (p->cu_seqlens_q || p->batch <= 0 || p->heads <= 0 || p->seqlen_q <= 0 ||
+      p->seqlen_kv <= 0 || splits_req == 1)
+    return sp;
+  const int64_t nq = (p->seqlen_q + fa8::kBlockM - 1) / fa8::kBlockM;
+  const int64_t n_kv = (p->seqlen_kv + fa8::kBlockN - 1) / fa8::kBlockN;
+  sp.qtiles = p->batch * p->heads * nq;
+  int64_t ns;
+  if (splits_req > 1) {
+    ns = splits_req;
+  } else {
+    // Split only when the grid would not fill the GPU and every share keeps
+    // at least kMinTilesPerSplit K/V tiles: each split CTA pays a partial
+    // round trip through the workspace and the last one a merge, which short
+    // shares do not earn back (B1 H8 S512: 13.7 us unsplit, 19-21 us split).
+    if (sp.qtiles >= kSmCount) return sp;  // the grid fills the GPU already
+    ns = std::min<int64_t>((2 * kSmCount + sp.qtiles - 1) / sp.qtiles,  // two CTAs per SM
+                           n_kv / kMinTilesPerSplit);
+  }
+  ns = std::min<int64_t>(std::min<int64_t>(ns, n_kv), kMaxSplits);
+  if (ns < 2 || p->batch * ns > 65535) return sp;
+  sp.splits = (int)ns;
+  const int64_t units = sp.qtiles * ns;
+  sp.cnt_bytes = (sp.qtiles * 4 + 255) / 256 * 256;
+  sp.lse_bytes = (units * fa8::kBlockM * 4 + 255) / 256 * 256;
+  sp.o_bytes = units * fa8::kBlockM * p->head_dim * 4;
+  return sp;
+}
+
 template <int D>
-int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
+int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev, const SplitPlan& sp) {
   using C = fa8::TileCfg<D>;
   int st = setup_kernel_attr<D>(dev);
   if (st) return st;
@@ -183,12 +225,22 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev) {
   kp.dq_sh = p->descale_q_stride_h;
   kp.dkv_sb = p->descale_kv_stride_b;
   kp.dkv_sh = p->descale_kv_stride_h;
+  kp.kv_splits = sp.splits;
+  kp.part_o = nullptr;
+  kp.part_lse = nullptr;
+  kp.split_cnt = nullptr;
+  if (sp.splits > 1) {
+    char* ws = static_cast<char*>(p->workspace);
+    kp.split_cnt = reinterpret_cast<unsigned int*>(ws);
+    kp.part_lse = reinterpret_cast<float*>(ws + sp.cnt_bytes);
+    kp.part_o = reinterpret_cast<float*>(ws + sp.cnt_bytes + sp.lse_bytes);
+  }
   if (varlen) {  // sequences are addressed by their packed row offsets
     kp.o_sb = 0;
     kp.lse_sb = 0;
   }
 
-  dim3 grid(kp.n_qblocks, (unsigned)p->heads, (unsigned)p->batch);
+  dim3 grid(kp.n_qblocks, (unsigned)p->heads, (unsigned)(p->batch * sp.splits));
   fa8::fa8_fwd_kernel<D><<<grid, fa8::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, to, kp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
@@ -298,7 +350,25 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
     return set_msg(FA8_ERR_NO_DEVICE, "the current device is not sm_100 (B200)");
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return p->head_dim == 128 ? launch<128>(p, s, dev) : launch<64>(p, s, dev);
+  if (p->kv_splits < 0) return set_msg(FA8_ERR_INVALID_ARG, "kv_splits must be >= 0");
+  SplitPlan sp = plan_splits(p, p->kv_splits);
+  if (sp.splits > 1) {
+    const bool fits = p->workspace && p->workspace_bytes >= sp.bytes() &&
+                      (reinterpret_cast<uintptr_t>(p->workspace) & 255) == 0;
+    if (!fits) {
+      if (p->kv_splits > 1)
+        return set_msg(FA8_ERR_INVALID_ARG,
+                       "kv_splits > 1 needs a 256-byte aligned workspace of "
+                       "fa8_fwd_workspace_size() bytes");
+      sp = SplitPlan();  // automatic: run without splitting
+    }
+  }
+  return p->head_dim == 128 ? launch<128>(p, s, dev, sp) : launch<64>(p, s, dev, sp);
+}
+
+int64_t fa8_fwd_workspace_size(const fa8_fwd_params* p) {
+  if (!p || p->kv_splits < 0 || (p->head_dim != 64 && p->head_dim != 128)) return 0;
+  return plan_splits(p, p->kv_splits).bytes();
 }
 
 const char* fa8_status_string(int status) {

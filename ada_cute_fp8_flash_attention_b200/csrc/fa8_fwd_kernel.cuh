@@ -80,11 +80,17 @@ constexpr int kRegsSoftmax = 192;
 static_assert(128 * kRegsControl + 128 * kRegsSoftmax <= 65536 / kMinBlocks,
               "setmaxnreg split exceeds the launch register budget");
 
-#ifndef FA8_EMU
-#define FA8_EMU 2
+#ifndef FA8_EMU128
+#define FA8_EMU128 2
 #endif
-// Columns of every 8 whose exp2 runs on the FMA pipe instead of MUFU.
-constexpr int kEmuPer8 = FA8_EMU;
+#ifndef FA8_EMU64
+#define FA8_EMU64 2
+#endif
+// Columns of every 8 whose exp2 runs on the FMA pipe instead of MUFU, per head
+// dimension (D = 64 has half the tensor work per step for the same number of
+// exponentials).
+template <int D>
+constexpr int kEmuPer8 = (D == 128) ? FA8_EMU128 : FA8_EMU64;
 #ifndef FA8_TMA_STORE
 #define FA8_TMA_STORE 1
 #endif
@@ -150,6 +156,15 @@ struct KernelParams {
   const float* dk_bh;
   const float* dv_bh;
   long long dq_sb, dq_sh, dkv_sb, dkv_sh;
+  // Split-KV (kv_splits > 1): grid.z = batch * kv_splits; split s of a query
+  // tile runs a contiguous share of its K/V tiles and writes a partial
+  // (O normalised by its own row sum, fp32, and its LSE) for the tile's last
+  // arriving split to merge. Unit u = qtile * kv_splits + s, qtile =
+  // (b * heads + h) * n_qblocks + qb.
+  int kv_splits;
+  float* part_o;             // [units][128][D]
+  float* part_lse;           // [units][128]
+  unsigned int* split_cnt;   // [qtiles], zero before the launch, left zero after it
 };
 
 #ifdef FA8_TRACE
@@ -185,7 +200,12 @@ struct Bars {
   uint64_t kv_empty[NS];
   uint64_t s_full;     // S(t) in TMEM (tcgen05.commit of the QK product)
   uint64_t s_free;     // the four softmax warps have read S(t)
-  uint64_t p_full;     // the four softmax warps have written P(t) (and rescaled O)
+  // The four softmax warps have written P(t) (and rescaled O): t even / odd.
+  // One barrier per P buffer: a warp may run a step ahead of a slower one
+  // (step t+1 only needs PV(t-1) and S(t+1)), and its arrival for P(t+1) must
+  // not count toward P(t). It cannot run two steps ahead: step t+2 waits for
+  // PV(t), which needs every warp's P(t).
+  uint64_t p_full[2];
   uint64_t o_done[2];  // PV(t) complete, t even / odd (the P buffer it read is free)
   uint64_t drain;      // every MMA of the MMA thread has completed
 };
@@ -303,6 +323,118 @@ __device__ __forceinline__ void store_o_chunk(const KernelParams& p, char* row_p
   }
 }
 
+constexpr int kMaxKvSplits = 16;
+
+// Store 4 consecutive O values (fp16, e4m3 or fp32) at element offset `col` of a row.
+__device__ __forceinline__ void store_o4(const KernelParams& p, char* row_ptr, int col,
+                                         float4 v) {
+  if (p.out_kind == 0) {
+    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    *reinterpret_cast<uint2*>(row_ptr + col * 2) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+  } else if (p.out_kind == 1) {
+    *reinterpret_cast<uint32_t*>(row_ptr + col) =
+        (uint32_t)ptx::cvt_e4m3x2(v.x, v.y) | ((uint32_t)ptx::cvt_e4m3x2(v.z, v.w) << 16);
+  } else {
+    *reinterpret_cast<float4*>(row_ptr + col * 4) = v;
+  }
+}
+
+// Split-KV tail, run by the 128 softmax threads of every split CTA after each
+// wrote its partial row: the last split of the query tile to arrive (atomic
+// counter) merges all partials by log-sum-exp,
+//   lse = log sum_s exp(lse_s),  O = sum_s exp(lse_s - lse) O_s,
+// writes the tile's O and LSE and resets the counter for the next launch.
+// The merge first turns each row's LSEs into weights (one thread per row,
+// kept in shared memory), then all 128 threads stream the partial rows in
+// float4 column groups so that many L2 reads are in flight at once.
+template <int D>
+__device__ __forceinline__ void split_finish(const KernelParams& p, long long qtile, int r,
+                                             int q_start, int sq, char* o_head, float* lse_head,
+                                             volatile int* last_sh,
+                                             float (*w_sh)[kBlockM]) {
+  const int ns = p.kv_splits;
+  __threadfence();  // this thread's partial row is visible device-wide
+  ptx::named_barrier_sync(3, kBlockM);
+  if (r == 0) {
+    const unsigned old = atomicAdd(p.split_cnt + qtile, 1u);
+    const int last = old == (unsigned)(ns - 1);
+    if (last) atomicExch(p.split_cnt + qtile, 0u);
+    *last_sh = last;
+  }
+  ptx::named_barrier_sync(3, kBlockM);
+  if (!*last_sh) return;
+  __threadfence();
+  const long long u0 = qtile * ns;
+  {
+    float l[kMaxKvSplits];
+    float m = -INFINITY;
+#pragma unroll
+    for (int sp = 0; sp < kMaxKvSplits; ++sp) {
+      l[sp] = sp < ns ? __ldcg(p.part_lse + (u0 + sp) * kBlockM + r) : -INFINITY;
+      m = fmaxf(m, l[sp]);
+    }
+    float wsum = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxKvSplits; ++sp) {
+      l[sp] = (m == -INFINITY || l[sp] == -INFINITY) ? 0.f : __expf(l[sp] - m);
+      wsum += l[sp];
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxKvSplits; ++sp)
+      if (sp < ns) w_sh[sp][r] = l[sp] * inv;
+    const int row = q_start + r;
+    if (lse_head && row < sq) lse_head[row] = wsum > 0.f ? m + __logf(wsum) : -INFINITY;
+  }
+  ptx::named_barrier_sync(3, kBlockM);
+  constexpr int kGroups = D / 4;  // float4 column groups per row
+  constexpr int kItems = kBlockM * kGroups / kBlockM;  // column groups per thread
+  constexpr int kBatch = 4;  // groups whose loads of every split are in flight together
+  static_assert(kItems % kBatch == 0, "batching of the merge");
+#pragma unroll 1
+  for (int i0 = 0; i0 < kItems; i0 += kBatch) {
+    float4 acc[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+    for (int s0 = 0; s0 < ns; s0 += 4) {
+      float4 x[4][kBatch];
+      float w[4][kBatch];
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const int i = (i0 + j) * kBlockM + r;
+          const int rr = i / kGroups, g = i % kGroups;
+          const bool in = s0 + sp < ns;
+          w[sp][j] = in ? w_sh[s0 + sp][rr] : 0.f;
+          x[sp][j] = in ? __ldcg(reinterpret_cast<const float4*>(
+                              p.part_o + ((u0 + s0 + sp) * kBlockM + rr) * D) + g)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int sp = 0; sp < 4; ++sp) {
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          acc[j].x += w[sp][j] * x[sp][j].x;
+          acc[j].y += w[sp][j] * x[sp][j].y;
+          acc[j].z += w[sp][j] * x[sp][j].z;
+          acc[j].w += w[sp][j] * x[sp][j].w;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = (i0 + j) * kBlockM + r;
+      const int rr = i / kGroups, g = i % kGroups;
+      const int row = q_start + rr;
+      if (row < sq) store_o4(p, o_head + (long long)row * p.o_ss * p.o_esize, g * 4, acc[j]);
+    }
+  }
+}
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, kMinBlocks)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -315,6 +447,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
   __shared__ int softmax_fail_sh;
+  __shared__ int split_last_sh;
+  __shared__ float split_w_sh[kMaxKvSplits][kBlockM];  // split-KV merge weights
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -327,9 +461,11 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     fa8_trace_cta[cta_lin][2] = smid;
   }
 #endif
+  if (lane == 0 && warp < 6) FA8_TR(warp < 4 ? warp : 4 + (warp == kLoadWarp), 62, 0);
   const int qb = p.causal ? (p.n_qblocks - 1 - (int)blockIdx.x) : (int)blockIdx.x;
   const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  const int b = blockIdx.z / p.kv_splits;
+  const int sidx = blockIdx.z % p.kv_splits;  // split of the K/V range (0 without split-KV)
   const int hk = h / p.head_group;
   // Variable-length batches: sequence b occupies rows [cu[b], cu[b+1]) of the
   // packed Q / O (and K / V^T) tensors; the TMA batch coordinate is then 0.
@@ -356,7 +492,19 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   }
 
   const TilePlan tp = plan_tile(p, qb, sq, skv);
-  const int n = tp.n;
+  // Split-KV: this CTA runs K/V tiles [t0, t0 + n) of the tile's processing
+  // order (tile kv_top - t at local step t).
+  int t0 = 0, n = tp.n;
+  if (p.kv_splits > 1) {
+    t0 = (int)((long long)tp.n * sidx / p.kv_splits);
+    n = (int)((long long)tp.n * (sidx + 1) / p.kv_splits) - t0;
+  }
+  const int kv_top = tp.n - 1 - t0;
+  const long long qtile = ((long long)b * p.heads + h) * p.n_qblocks + qb;
+  float* const part_o_row0 =
+      p.kv_splits > 1 ? p.part_o + (qtile * p.kv_splits + sidx) * kBlockM * D : nullptr;
+  float* const part_lse0 =
+      p.kv_splits > 1 ? p.part_lse + (qtile * p.kv_splits + sidx) * kBlockM : nullptr;
 
   char* o_head = reinterpret_cast<char*>(p.o) +
                  ((long long)b * p.o_sb + (long long)h * p.o_sh + (long long)q_base * p.o_ss) *
@@ -364,6 +512,18 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   float* lse_head =
       p.lse ? p.lse + (long long)b * p.lse_sb + (long long)h * p.lse_sh + q_base : nullptr;
 
+  if (n == 0 && p.kv_splits > 1) {
+    // An empty share of a split query tile: an empty partial, then the merge.
+    if (warp < kSoftmaxWarps) {
+      const int r = threadIdx.x;
+      float4* dst = reinterpret_cast<float4*>(part_o_row0 + (long long)r * D);
+#pragma unroll
+      for (int j = 0; j < D / 4; ++j) dst[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      part_lse0[r] = -INFINITY;
+      split_finish<D>(p, qtile, r, tp.q_start, sq, o_head, lse_head, &split_last_sh, split_w_sh);
+    }
+    return;
+  }
   if (n == 0) {
     // Every row of this CTA is fully masked (or past the sequence): O = 0, LSE = -inf.
     if (warp < kSoftmaxWarps) {
@@ -390,7 +550,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     ptx::mbar_init(&bars.q_full, 1);
     ptx::mbar_init(&bars.s_full, 1);
     ptx::mbar_init(&bars.s_free, kSoftmaxWarps);
-    ptx::mbar_init(&bars.p_full, kSoftmaxWarps);
+    ptx::mbar_init(&bars.p_full[0], kSoftmaxWarps);
+    ptx::mbar_init(&bars.p_full[1], kSoftmaxWarps);
     ptx::mbar_init(&bars.o_done[0], 1);
     ptx::mbar_init(&bars.o_done[1], 1);
     ptx::mbar_init(&bars.drain, 1);
@@ -412,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   ptx::tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
   volatile int* abort_flag = &abort_sh;
+  if (lane == 0 && warp < 6) FA8_TR(warp < 4 ? warp : 4 + (warp == kLoadWarp), 62, 1);
 
   if (warp >= kSoftmaxWarps) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
@@ -430,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         bool is_v;
         int t;
         load_slot_inverse(L, n, is_v, t);
-        const int kv = n - 1 - t;
+        const int kv = kv_top - t;
         const int st = L % NS;
         if (L >= NS)
           ok = bounded_wait(&bars.kv_empty[st], ((L / NS) - 1) & 1, abort_flag, p.status,
@@ -500,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
           ok = bounded_wait(&bars.kv_full[st], (L / NS) & 1, abort_flag, p.status, p.timeout_cycles);
           if (!ok) break;
           FA8_TR(4, t + 1, 4);
-          ok = bounded_wait(&bars.p_full, t & 1, abort_flag, p.status, p.timeout_cycles);
+          ok = bounded_wait(&bars.p_full[t & 1], (t >> 1) & 1, abort_flag, p.status, p.timeout_cycles);
           if (!ok) break;
           ptx::tc_fence_after();
           FA8_TR(4, t + 1, 7);
@@ -575,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     };
 
     for (int tl = 0; tl < n && ok; ++tl) {
-      const int kv = n - 1 - tl;
+      const int kv = kv_top - tl;
       if (lane == 0) FA8_TR(warp, tl, 0);
       ok = bounded_wait(&bars.s_full, tl & 1, abort_flag, p.status, p.timeout_cycles);
       if (lane == 0) FA8_TR(warp, tl, 1);
@@ -620,11 +782,11 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         // code. D = 128: P is converted inside the exp loop and each 16-byte
         // chunk goes to shared memory at once.
         if constexpr (!C::kPInTmem)
-          so = softmax_row_step<kBlockN, kEmuPer8, true, true>(
+          so = softmax_row_step<kBlockN, kEmuPer8<D>, true, true>(
               s, sl2, tl == 0, false, m_run, l_run, ph, pl,
               s_base + C::kOffP + buf * C::kPBytes + r * 128, swz);
         else
-          so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, false, m_run, l_run, ph, pl);
+          so = softmax_row_step<kBlockN, kEmuPer8<D>>(s, sl2, tl == 0, false, m_run, l_run, ph, pl);
       } else {
         // Mask: keys past seqlen_kv, and (causal) keys after this query.
         long long lim = skv - kv0;
@@ -635,7 +797,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
           for (int c = 0; c < kBlockN; ++c)
             if (c >= li) s[c] = -INFINITY;
         }
-        so = softmax_row_step<kBlockN, kEmuPer8>(s, sl2, tl == 0, split, m_run, l_run, ph, pl);
+        so = softmax_row_step<kBlockN, kEmuPer8<D>>(s, sl2, tl == 0, split, m_run, l_run, ph, pl);
       }
 #ifdef FA8_TRACE
       {
@@ -699,13 +861,15 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
       }
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&bars.p_full);
+      if (lane == 0) ptx::mbar_arrive(&bars.p_full[tl & 1]);
       if (lane == 0) FA8_TR(warp, tl, 5);
     }
     ok = __all_sync(0xffffffffu, ok);
 
     // Epilogue: O / l -> global, LSE.
+    if (lane == 0) FA8_TR(warp, 62, 2);
     if (ok) ok = wait_pv(n - 1);
+    if (lane == 0) FA8_TR(warp, 62, 3);
     ok = __all_sync(0xffffffffu, ok);
     // One CTA-wide verdict for the four softmax warps (the TMA-store path
     // below has a barrier that all of them must reach).
@@ -718,9 +882,30 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     // the P tiles (idle once the last PV completed) in the 128B-swizzled box
     // layout, one thread issues the stores. Tiles that end past the sequence (ragged /
     // varlen), e4m3 output and aborted CTAs take per-thread global stores.
-    const bool tma_out =
-        kTmaStore && p.o_tma && p.out_kind == 0 && ok && tp.q_start + kBlockM <= sq;
-    if (tma_out) {
+    const bool tma_out = kTmaStore && p.o_tma && p.out_kind == 0 && ok &&
+                         tp.q_start + kBlockM <= sq && p.kv_splits == 1;
+    if (p.kv_splits > 1) {
+      // Partial of this split: O / l (fp32) and its LSE; the merge follows below.
+      float4* dst = reinterpret_cast<float4*>(part_o_row0 + (long long)r * D);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t u[32];
+        ptx::tmem_ld32(t_o + c * 32, u);
+        ptx::tmem_wait_ld();
+        ptx::reg_fence32(u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          dst[c * 8 + j] = ok ? make_float4(__uint_as_float(u[4 * j]) * inv_l,
+                                            __uint_as_float(u[4 * j + 1]) * inv_l,
+                                            __uint_as_float(u[4 * j + 2]) * inv_l,
+                                            __uint_as_float(u[4 * j + 3]) * inv_l)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      const float base = m_run - kPShift;
+      part_lse0[r] =
+          (l_run > 0.f && ok) ? (__log2f(l_run) + base) * 0.69314718055994531f : -INFINITY;
+      split_finish<D>(p, qtile, r, tp.q_start, sq, o_head, lse_head, &split_last_sh, split_w_sh);
+    } else if (tma_out) {
 #pragma unroll
       for (int hb = 0; hb < D / 64; ++hb) {
         // box hb = columns [64 hb, 64 hb + 64): 128 rows x 128 B
@@ -769,13 +954,14 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         if (row < sq) store_o_chunk(p, row_ptr, c, v);
       }
     }
-    if (lse_head && row < sq) {
+    if (lse_head && row < sq && p.kv_splits == 1) {
       const float base = m_run - kPShift;
       lse_head[row] =
           (l_run > 0.f && ok) ? (__log2f(l_run) + base) * 0.69314718055994531f : -INFINITY;
     }
   }
 
+  if (lane == 0 && warp < 6) FA8_TR(warp < 4 ? warp : 4 + (warp == kLoadWarp), 62, 4);
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -783,6 +969,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, C::kTmemCols);
   }
+  if (lane == 0 && warp < 6) FA8_TR(warp < 4 ? warp : 4 + (warp == kLoadWarp), 62, 5);
 #ifdef FA8_TRACE
   if (threadIdx.x == 0 && cta_lin < 4096) fa8_trace_cta[cta_lin][1] = fa8_gtimer();
 #endif

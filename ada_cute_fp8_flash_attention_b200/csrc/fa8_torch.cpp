@@ -177,6 +177,18 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
   p.descale_q_stride_h = 1;
   p.descale_kv_stride_b = Hkv;
   p.descale_kv_stride_h = 1;
+  // Split-KV for calls too small to fill the GPU: a workspace from the caching
+  // allocator whose leading counters start at zero.
+  torch::Tensor ws;
+  p.kv_splits = 0;
+  const int64_t ws_bytes = fa8_fwd_workspace_size(&p);
+  if (ws_bytes > 0) {
+    ws = torch::empty({ws_bytes}, q.options().dtype(at::kByte));
+    const int64_t qtiles = B * H * ((Sq + 127) / 128);
+    ws.narrow(0, 0, (qtiles * 4 + 255) / 256 * 256).zero_();
+    p.workspace = ws.data_ptr();
+    p.workspace_bytes = ws_bytes;
+  }
   check_status(fa8_fwd(&p, stream.stream()), "fa8_fwd");
   if (lse.defined()) return {out, lse};
   return {out};

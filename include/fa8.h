@@ -147,6 +147,23 @@ typedef struct fa8_fwd_params {
   int64_t descale_q_stride_h;
   int64_t descale_kv_stride_b;
   int64_t descale_kv_stride_h;
+
+  /* Split-KV (no counterpart in the reference, which launches one CTA per
+   * 64-row query block): when a call has fewer query tiles than the GPU has
+   * SMs, each 128-row query tile's K/V range is cut into kv_splits shares run
+   * by separate CTAs, and the last share to finish merges the partial
+   * outputs by log-sum-exp inside the same launch. kv_splits: 0 = automatic
+   * (split only when the grid would not fill the GPU and `workspace` is large
+   * enough, see fa8_fwd_workspace_size), 1 = never, n > 1 = up to n shares
+   * (FA8_ERR_INVALID_ARG if the workspace is too small). workspace: device
+   * memory, 256-byte aligned, of workspace_bytes bytes; its first
+   * 256 * ceil(4 * query_tiles / 256) bytes are counters that must be zero
+   * before the first call (the kernel leaves them zero; after a call that
+   * reported FA8_DEVERR_TIMEOUT, zero them again). Not used for varlen calls. */
+  void* workspace;
+  int64_t workspace_bytes;
+  int32_t kv_splits;
+  int32_t reserved3;
 } fa8_fwd_params;
 
 /* Fill *p with defaults: contiguous strides for the given shape, scale
@@ -159,6 +176,11 @@ void fa8_fwd_params_init(fa8_fwd_params* p, int64_t batch, int64_t heads,
 /* Launch the forward on `stream` (a cudaStream_t, NULL = legacy default).
  * Asynchronous; returns after the launch is queued. */
 int fa8_fwd(const fa8_fwd_params* p, void* stream);
+
+/* Workspace bytes fa8_fwd would use for split-KV with these parameters
+ * (kv_splits 0 or n > 1); 0 when the call does not split. Host-only, no
+ * device access. No counterpart in the reference. */
+int64_t fa8_fwd_workspace_size(const fa8_fwd_params* p);
 
 /*
  * Log-sum-exp merge of `n_parts` partial attention outputs of the same rows:

@@ -98,3 +98,63 @@ def test_quantize_matches_torch_cast(abi, cuda, transpose):
     if transpose:
         ref = ref.transpose(-1, -2).contiguous()
     assert torch.equal(y.cpu(), ref.view(torch.uint8).cpu())
+
+
+def _fwd_splits(abi, q, k, v, causal, device, kv_splits, ws=None, lse=True):
+    import torch
+    B, H, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    out = torch.full((B, H, Sq, D), 9.0, dtype=torch.float16, device=device)
+    l = torch.empty((B, H, Sq), dtype=torch.float32, device=device)
+    p = abi.params(B, H, Hkv, Sq, Skv, D)
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    p.lse = l.data_ptr() if lse else None
+    p.causal = int(causal)
+    p.kv_splits = kv_splits
+    need = abi.workspace_size(p)
+    if need and ws is not None:
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    abi.check(abi.fwd(p, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return out, l, need
+
+
+@pytest.mark.parametrize("D,causal,Sq,Skv,splits", [
+    (64, False, 512, 512, 3), (128, False, 1008, 1008, 2), (128, True, 512, 512, 4),
+    (64, True, 1024, 1024, 8),
+    (128, False, 128, 4096, 0),    # decode-like: automatic split (few query tiles, long K/V)
+    (64, True, 256, 8192, 0),      # causal with offsets: some shares see no keys
+])
+def test_split_kv_matches_the_unsplit_kernel(abi, cuda, D, causal, Sq, Skv, splits):
+    """Split-KV (partials merged in-kernel by the last share) == one CTA per tile."""
+    import torch
+    q, k, v = U.inputs(1, 2, 2, Sq, Skv, D, "normal", seed=Sq + Skv + D)
+    qd, kd, vd = U.to_dev(q, cuda), U.to_dev(k, cuda), U.to_dev(v, cuda)
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device=cuda)
+    o1, l1, need1 = _fwd_splits(abi, qd, kd, vd, causal, cuda, 1)
+    assert need1 == 0
+    o_ref, _ = U.oracle(q, k, v, causal)
+    for _ in range(2):  # twice: the counters must come back to zero
+        o2, l2, need = _fwd_splits(abi, qd, kd, vd, causal, cuda, splits, ws)
+        assert need > 0
+        assert (o2.float() - o1.float()).abs().max().item() < U.MAX_ABS
+        fin = torch.isfinite(l1)
+        assert torch.equal(fin, torch.isfinite(l2))
+        assert (l2[fin] - l1[fin]).abs().max().item() < 1e-3
+        U.assert_close(o2.float().cpu().numpy(), o_ref)
+    qtiles = 2 * ((Sq + 127) // 128)
+    assert int(ws[:qtiles * 4].sum().item()) == 0, "split counters must be left at zero"
+
+
+def test_split_kv_needs_a_workspace(abi, cuda):
+    import torch
+    q = torch.zeros((1, 1, 256, 64), dtype=torch.float8_e4m3fn, device=cuda)
+    p = abi.params(1, 1, 1, 256, 256, 64)
+    p.q = p.k = p.v = q.data_ptr()
+    out = torch.empty((1, 1, 256, 64), dtype=torch.float16, device=cuda)
+    p.o = out.data_ptr()
+    p.kv_splits = 2
+    assert abi.fwd(p) == abi.FA8_ERR_INVALID_ARG  # explicit split without workspace
+    p.kv_splits = 0
+    assert abi.fwd(p) == abi.FA8_OK  # automatic: falls back to no split
+    torch.cuda.synchronize()

@@ -288,3 +288,20 @@ def test_varlen_needs_no_host_sync(fa8, cuda):
         torch.cuda.set_sync_debug_mode(prev)
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("B,H,S,D,causal", [(4, 32, 2048, 128, False), (8, 32, 2048, 128, True),
+                                            (16, 16, 1024, 64, False), (4, 8, 1024, 64, True)])
+def test_repeated_launches_are_bit_identical(fa8, cuda, B, H, S, D, causal):
+    """Many CTAs per SM over many steps: every launch gives the same bits. A
+    softmax warp may run one step ahead of the others; a hand-off that let its
+    arrival count for the previous step showed up as launch-to-launch drift."""
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(5)
+    q = torch.randn((B, H, S, D), generator=g, device=cuda).to(torch.float8_e4m3fn)
+    k = torch.randn((B, H, S, D), generator=g, device=cuda).to(torch.float8_e4m3fn)
+    v = torch.randn((B, H, D, S), generator=g, device=cuda).to(torch.float8_e4m3fn)
+    first = fa8.flash_attn_fp8_forward_ex(q, k, v, causal=causal)
+    for _ in range(12):
+        again = fa8.flash_attn_fp8_forward_ex(q, k, v, causal=causal)
+        assert torch.equal(first, again)
