@@ -28,6 +28,8 @@ EXPORTED = [
     "fa8_fwd_params_init",
     "fa8_fwd",
     "fa8_fwd_workspace_size",
+    "fa8_fwd_static_scratch",
+    "fa8_static_scratch_bytes",
     "fa8_lse_merge",
     "fa8_quantize_e4m3",
     "fa8_status_string",
@@ -80,6 +82,10 @@ def lib(path: Path | None = None) -> C.CDLL:
         L.fa8_fwd.restype = C.c_int
         L.fa8_fwd_workspace_size.argtypes = [C.POINTER(Fa8FwdParams)]
         L.fa8_fwd_workspace_size.restype = C.c_int64
+        L.fa8_fwd_static_scratch.argtypes = [C.POINTER(Fa8FwdParams), C.c_void_p]
+        L.fa8_fwd_static_scratch.restype = C.c_int
+        L.fa8_static_scratch_bytes.argtypes = []
+        L.fa8_static_scratch_bytes.restype = C.c_int64
         L.fa8_lse_merge.argtypes = [C.c_int, C.POINTER(C.c_void_p), C.c_int,
                                     C.POINTER(C.c_void_p), C.c_int64, C.c_int64, C.c_void_p,
                                     C.c_int64, C.c_void_p, C.c_void_p]
@@ -114,6 +120,11 @@ def check(status: int) -> None:
 
 def fwd(p: Fa8FwdParams, stream: int = 0) -> int:
     return lib().fa8_fwd(C.byref(p), C.c_void_p(stream))
+
+
+def fwd_static_scratch(p: Fa8FwdParams, stream: int = 0) -> int:
+    """fa8_fwd for callers that cannot allocate: split-KV scratch from the library's fixed array."""
+    return lib().fa8_fwd_static_scratch(C.byref(p), C.c_void_p(stream))
 
 
 def workspace_size(p: Fa8FwdParams) -> int:

@@ -371,6 +371,79 @@ int64_t fa8_fwd_workspace_size(const fa8_fwd_params* p) {
   return plan_splits(p, p->kv_splits).bytes();
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Forward for callers that cannot allocate device memory.
+//
+// Split-KV needs scratch (the shares' partial outputs and the per-tile
+// counters). fa8_fwd takes it from the caller; some callers have no way to
+// provide it: code running inside a framework that owns the device memory
+// pool, plugins that may not call cudaMalloc (or may not call it from the
+// thread that launches), and runtimes whose launch path must not allocate.
+// fa8_fwd_static_scratch gives them the same forward with the scratch taken
+// from this fixed-size array, which is part of the library's image: every GPU
+// that loads the library holds it until the process exits.
+namespace {
+
+constexpr int64_t kStaticScratchBytes = 8ll << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on `dev`, looked up once per device with
+// that device current. In host code the symbol itself is only a host-side
+// stand-in: it must never be passed to a kernel as a pointer.
+int static_scratch_ptr(int dev, void** out) {
+  static std::once_flag flags[64];
+  static void* ptrs[64];
+  static cudaError_t errs[64];
+  if (dev < 0 || dev >= 64) return set_msg(FA8_ERR_INVALID_ARG, "device index out of range");
+  std::call_once(flags[dev], [dev] {
+    errs[dev] = cudaGetSymbolAddress(&ptrs[dev], g_static_scratch);
+  });
+  if (errs[dev] != cudaSuccess) return set_cuda_error(errs[dev], "cudaGetSymbolAddress");
+  *out = ptrs[dev];
+  return FA8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa8_fwd_static_scratch(const fa8_fwd_params* p, void* stream) {
+  if (!p) return set_msg(FA8_ERR_INVALID_ARG, "params is NULL");
+  if (p->kv_splits < 0) return set_msg(FA8_ERR_INVALID_ARG, "kv_splits must be >= 0");
+  fa8_fwd_params q = *p;
+  q.workspace = nullptr;
+  q.workspace_bytes = 0;
+  const int64_t need = fa8_fwd_workspace_size(&q);
+  if (need > kStaticScratchBytes) {
+    snprintf(g_last_msg, sizeof(g_last_msg),
+             "fa8_fwd_static_scratch: this call's split-KV plan needs %lld bytes of scratch, "
+             "more than the library's fixed %lld; pass kv_splits = 1 (no split) or call "
+             "fa8_fwd with a workspace",
+             (long long)need, (long long)kStaticScratchBytes);
+    return FA8_ERR_INVALID_ARG;
+  }
+  if (need > 0) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaGetDevice");
+    void* ptr = nullptr;
+    const int st = static_scratch_ptr(dev, &ptr);
+    if (st) return st;
+    // The array keeps the previous call's contents; the split counters at its
+    // start must be zero (a call that timed out can leave them set).
+    const SplitPlan sp = plan_splits(&q, q.kv_splits);
+    e = cudaMemsetAsync(ptr, 0, (size_t)sp.cnt_bytes, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaMemsetAsync (split counters)");
+    q.workspace = ptr;
+    q.workspace_bytes = kStaticScratchBytes;
+  }
+  return fa8_fwd(&q, stream);
+}
+
+int64_t fa8_static_scratch_bytes(void) { return kStaticScratchBytes; }
+
 const char* fa8_status_string(int status) {
   switch (status) {
     case FA8_OK: return "ok";

@@ -183,6 +183,26 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream);
 int64_t fa8_fwd_workspace_size(const fa8_fwd_params* p);
 
 /*
+ * The forward for callers that cannot allocate device memory (no counterpart
+ * in the reference). Split-KV needs scratch that fa8_fwd takes from the
+ * caller's `workspace`; code that runs inside a framework owning the memory
+ * pool, plugins forbidden to call cudaMalloc, or launch paths that must not
+ * allocate cannot provide one. This entry point ignores `workspace` /
+ * `workspace_bytes` and uses a scratch array compiled into the library
+ * (fa8_static_scratch_bytes() = 8 MiB, resident on every GPU that loads the
+ * library until the process exits). It allocates nothing: it rejects a call
+ * whose split plan needs more than that with FA8_ERR_INVALID_ARG (use
+ * kv_splits = 1, or fa8_fwd with a workspace), and otherwise clears the split
+ * counters with an asynchronous memset on `stream` and calls fa8_fwd. The
+ * first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. All calls
+ * share the one array: calls whose kernels overlap on the GPU (other streams,
+ * other threads) race on it and must be serialised by the caller.
+ */
+int fa8_fwd_static_scratch(const fa8_fwd_params* p, void* stream);
+int64_t fa8_static_scratch_bytes(void);
+
+/*
  * Log-sum-exp merge of `n_parts` partial attention outputs of the same rows:
  *   lse = log(sum_i exp(lse_i)), o = sum_i exp(lse_i - lse) * o_i.
  * o_parts: n_parts pointers to fp32 [rows][head_dim] or fp16 (o_is_f16);
