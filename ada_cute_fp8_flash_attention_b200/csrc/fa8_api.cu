@@ -76,13 +76,13 @@ int make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t row
   return FA8_OK;
 }
 
-template <int D>
+template <int D, bool kVmn>
 int setup_kernel_attr(int dev) {
   static std::once_flag flags[64];
   static cudaError_t errs[64];
   if (dev < 0 || dev >= 64) return set_msg(FA8_ERR_INVALID_ARG, "device index out of range");
   std::call_once(flags[dev], [dev] {
-    errs[dev] = cudaFuncSetAttribute(fa8::fa8_fwd_kernel<D>,
+    errs[dev] = cudaFuncSetAttribute(fa8::fa8_fwd_kernel<D, kVmn>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      fa8::TileCfg<D>::kSmemAlloc);
   });
@@ -136,7 +136,8 @@ SplitPlan plan_splits(const fa8_fwd_params* p, int splits_req) {
 template <int D>
 int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev, const SplitPlan& sp) {
   using C = fa8::TileCfg<D>;
-  int st = setup_kernel_attr<D>(dev);
+  int st = setup_kernel_attr<D, false>(dev);
+  if (!st) st = setup_kernel_attr<D, true>(dev);
   if (st) return st;
   const CUtensorMapSwizzle swz_qk =
       (D == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -203,7 +204,6 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev, const SplitPla
   kp.cu_seqlens_q = p->cu_seqlens_q;
   kp.cu_seqlens_kv = p->cu_seqlens_kv;
   kp.o_tma = o_tma ? 1 : 0;
-  kp.v_bhsd = v_bhsd ? 1 : 0;
   kp.scale_log2 = p->softmax_scale * p->descale_q * p->descale_k * 1.4426950408889634f;
   kp.o_scale = p->descale_v;
   kp.q_offset = p->q_offset;
@@ -241,7 +241,10 @@ int launch(const fa8_fwd_params* p, cudaStream_t stream, int dev, const SplitPla
   }
 
   dim3 grid(kp.n_qblocks, (unsigned)p->heads, (unsigned)(p->batch * sp.splits));
-  fa8::fa8_fwd_kernel<D><<<grid, fa8::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, to, kp);
+  if (v_bhsd)
+    fa8::fa8_fwd_kernel<D, true><<<grid, fa8::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, to, kp);
+  else
+    fa8::fa8_fwd_kernel<D, false><<<grid, fa8::kThreads, C::kSmemAlloc, stream>>>(tq, tk, tv, to, kp);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "fa8_fwd_kernel launch");

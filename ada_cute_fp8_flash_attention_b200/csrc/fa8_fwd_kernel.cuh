@@ -91,6 +91,22 @@ static_assert(128 * kRegsControl + 128 * kRegsSoftmax <= 65536 / kMinBlocks,
 // exponentials).
 template <int D>
 constexpr int kEmuPer8 = (D == 128) ? FA8_EMU128 : FA8_EMU64;
+#ifndef FA8_PDBL128
+#define FA8_PDBL128 1
+#endif
+#ifndef FA8_PDBL64
+#define FA8_PDBL64 0
+#endif
+#ifndef FA8_STREAM128
+#define FA8_STREAM128 1
+#endif
+// Double-buffered P (buffer t & 1; writing P(t) waits for PV(t-2)) or one
+// buffer (writing P(t) waits for PV(t-1)); streamed e4m3 stores during the exp
+// loop for D = 128 (with one buffer they wait for PV(t-1) before the loop).
+template <int D>
+constexpr bool kPDouble = (D == 128) ? FA8_PDBL128 != 0 : FA8_PDBL64 != 0;
+template <int D>
+constexpr bool kPStream = D == 128 && FA8_STREAM128 != 0;
 #ifndef FA8_TMA_STORE
 #define FA8_TMA_STORE 1
 #endif
@@ -149,7 +165,6 @@ struct KernelParams {
   const int* cu_seqlens_q;   // varlen: (batch + 1) prefix sums, or null
   const int* cu_seqlens_kv;
   int o_tma;                 // tm_o describes O (fp16, 16-byte aligned strides)
-  int v_bhsd;                // tm_v describes V as (B, H_kv, S, D) tiles of 128 keys x D
   long long timeout_cycles;  // bound of every barrier wait
   int debug_skip_kv_loads;   // test hook: issue no K/V loads (waits run out)
   const float* dq_bh;        // optional per-(batch, head) dequant factors
@@ -435,7 +450,9 @@ __device__ __forceinline__ void split_finish(const KernelParams& p, long long qt
   }
 }
 
-template <int D>
+// kVmn: V stored (B, H_kv, S, D) and read as an MN-major operand (a
+// template parameter so that the MMA issue path carries no layout branch).
+template <int D, bool kVmn>
 __global__ void __launch_bounds__(kThreads, kMinBlocks)
     fa8_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v,
@@ -448,7 +465,6 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   __shared__ int abort_sh;
   __shared__ int softmax_fail_sh;
   __shared__ int split_last_sh;
-  __shared__ float split_w_sh[kMaxKvSplits][kBlockM];  // split-KV merge weights
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -512,6 +528,11 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   float* lse_head =
       p.lse ? p.lse + (long long)b * p.lse_sb + (long long)h * p.lse_sh + q_base : nullptr;
 
+  // Split-KV merge weights live in the P tiles, idle by the time of the merge.
+  float (*const split_w)[kBlockM] = reinterpret_cast<float (*)[kBlockM]>(
+      ((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023)) +
+      TileCfg<D>::kOffP);
+  static_assert(kMaxKvSplits * kBlockM * 4 <= TileCfg<D>::kPBytes, "merge weights fit a P tile");
   if (n == 0 && p.kv_splits > 1) {
     // An empty share of a split query tile: an empty partial, then the merge.
     if (warp < kSoftmaxWarps) {
@@ -520,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 #pragma unroll
       for (int j = 0; j < D / 4; ++j) dst[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       part_lse0[r] = -INFINITY;
-      split_finish<D>(p, qtile, r, tp.q_start, sq, o_head, lse_head, &split_last_sh, split_w_sh);
+      split_finish<D>(p, qtile, r, tp.q_start, sq, o_head, lse_head, &split_last_sh, split_w);
     }
     return;
   }
@@ -603,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         if (!is_v)
           ptx::tma_load_4d(dst, &tm_k, &bars.kv_full[st], 0, kv_base + kv * kBlockN, hk, tb,
                            pol_kv);
-        else if (!p.v_bhsd)
+        else if (!kVmn)
           ptx::tma_load_4d(dst, &tm_v, &bars.kv_full[st], kv_base + kv * kBlockN, 0, hk, tb,
                            pol_kv);
         else
@@ -668,12 +689,12 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
           FA8_TR(4, t + 1, 7);
           const uint32_t v_addr = s_base + C::kOffRing + st * C::kStageBytes;
           const uint32_t d_tmem = tmem + C::kColO;
-          const int hi_buf = split ? 0 : (t & 1);
+          const int hi_buf = (split || !kPDouble<D>) ? 0 : (t & 1);
           // B = V: K-major V^T tile (D rows of 128 keys) or MN-major V tile
           // (128 rows of D); one K step is 32 keys.
-          const uint32_t idesc_o = p.v_bhsd ? C::kIdescOmn : C::kIdescO;
+          constexpr uint32_t idesc_o = kVmn ? C::kIdescOmn : C::kIdescO;
           auto desc_v = [&](int kk) -> uint64_t {
-            return p.v_bhsd ? ptx::smem_desc_mnmajor(v_addr + kk * 32 * D, D)
+            return kVmn ? ptx::smem_desc_mnmajor(v_addr + kk * 32 * D, D)
                             : ptx::smem_desc_kmajor(v_addr + kk * 32, 128);
           };
           if constexpr (C::kPInTmem) {
@@ -768,10 +789,16 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
           (kv0 + kBlockN > skv) ||
           (p.causal && p.kv_offset + kv0 + kBlockN - 1 > p.q_offset + tp.q_start);
       // P buffer of this step: t & 1 (hi and lo use buffers 0 and 1 when split).
-      const int buf = split ? 0 : (tl & 1);
-      if (!split && tl >= 2) {
+      const bool dbl = kPDouble<D> && !split;
+      const int buf = dbl ? (tl & 1) : 0;
+      const bool streamed = kPStream<D> && !tile_masked && !split && !C::kPInTmem;
+      if (dbl && tl >= 2) {
         // The buffer was read by PV(t-2).
         ok = wait_pv(tl - 2);
+        if (!ok) break;
+      } else if (!dbl && streamed && tl >= 1) {
+        // One buffer, written during the exp loop: PV(t-1) must have read it.
+        ok = wait_pv(tl - 1);
         if (!ok) break;
       }
       uint32_t ph[kBlockN / 4];
@@ -781,10 +808,13 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
         // Hot path: an unmasked K/V tile, single-term P — no mask or split
         // code. D = 128: P is converted inside the exp loop and each 16-byte
         // chunk goes to shared memory at once.
-        if constexpr (!C::kPInTmem)
+        if constexpr (kPStream<D> && !C::kPInTmem)
           so = softmax_row_step<kBlockN, kEmuPer8<D>, true, true>(
               s, sl2, tl == 0, false, m_run, l_run, ph, pl,
               s_base + C::kOffP + buf * C::kPBytes + r * 128, swz);
+        else if constexpr (!C::kPInTmem)
+          so = softmax_row_step<kBlockN, kEmuPer8<D>, true>(s, sl2, tl == 0, false, m_run, l_run,
+                                                           ph, pl);
         else
           so = softmax_row_step<kBlockN, kEmuPer8<D>>(s, sl2, tl == 0, false, m_run, l_run, ph, pl);
       } else {
@@ -810,12 +840,11 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 #endif
       const bool need = so.need;
       const float alpha = so.alpha;
-      const bool streamed = !tile_masked && !split && !C::kPInTmem;
 
       if (lane == 0) FA8_TR(warp, tl, 3);
       // O may only be rescaled once PV(t-1) is complete; split tiles also
       // reuse PV(t-1)'s buffers.
-      if (tl > 0 && (need || split)) {
+      if (tl > 0 && (need || !dbl)) {
         ok = wait_pv(tl - 1);
         if (!ok) break;
         if (lane == 0) FA8_TR(warp, tl, 4);
@@ -904,7 +933,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
       const float base = m_run - kPShift;
       part_lse0[r] =
           (l_run > 0.f && ok) ? (__log2f(l_run) + base) * 0.69314718055994531f : -INFINITY;
-      split_finish<D>(p, qtile, r, tp.q_start, sq, o_head, lse_head, &split_last_sh, split_w_sh);
+      split_finish<D>(p, qtile, r, tp.q_start, sq, o_head, lse_head, &split_last_sh, split_w);
     } else if (tma_out) {
 #pragma unroll
       for (int hb = 0; hb < D / 64; ++hb) {

@@ -34,6 +34,9 @@ static_assert(kPShift + kRescaleThreshold <= 8.8f, "largest P must stay below e4
 #ifndef FA8_FUSED_CVT
 #define FA8_FUSED_CVT 1
 #endif
+#ifndef FA8_MAX_TREE
+#define FA8_MAX_TREE 1
+#endif
 #ifndef FA8_EMU_DEG
 #define FA8_EMU_DEG 3
 #endif
@@ -103,6 +106,32 @@ __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, b
   static_assert(!kStream || (kFuse && NC == 128), "streamed P stores need the fused loop");
   static_assert(NC % 16 == 0, "row length must be a multiple of 16");
   // 1. row max
+#if FA8_MAX_TREE
+  // Balanced three-input max tree: the same instruction count as the chains
+  // below, dependency depth about log3(NC) instead of NC / 16 + 3.
+  float mx;
+  {
+    float l1[(NC + 2) / 3];
+#pragma unroll
+    for (int i = 0; i < NC / 3; ++i) l1[i] = ptx::fmax3(s[3 * i], s[3 * i + 1], s[3 * i + 2]);
+    constexpr int n1 = NC / 3 + (NC % 3 ? 1 : 0);
+    if constexpr (NC % 3 == 1) l1[n1 - 1] = s[NC - 1];
+    if constexpr (NC % 3 == 2) l1[n1 - 1] = fmaxf(s[NC - 2], s[NC - 1]);
+    int n = n1;
+#pragma unroll
+    for (int level = 0; level < 6; ++level) {
+      if (n <= 1) break;
+      const int m = n / 3, rem = n % 3;
+#pragma unroll
+      for (int i = 0; i < (NC + 2) / 3; ++i)
+        if (i < m) l1[i] = ptx::fmax3(l1[3 * i], l1[3 * i + 1], l1[3 * i + 2]);
+      if (rem == 1) l1[m] = l1[n - 1];
+      if (rem == 2) l1[m] = fmaxf(l1[n - 2], l1[n - 1]);
+      n = m + (rem ? 1 : 0);
+    }
+    mx = l1[0];
+  }
+#else
   constexpr int G = NC / 16;
   float mxg[G];
 #pragma unroll
@@ -115,6 +144,7 @@ __device__ __forceinline__ StepOut softmax_row_step(float (&s)[NC], float sl2, b
   float mx = mxg[0];
 #pragma unroll
   for (int g = 1; g < G; ++g) mx = fmaxf(mx, mxg[g]);
+#endif
 
   // 2. lazy rescale decision
   StepOut out;

@@ -12,6 +12,7 @@ import math
 import numpy as np
 import pytest
 
+from oracle import attention_ref as ref
 from tests import _util as U
 
 pytestmark = pytest.mark.gpu
@@ -305,3 +306,45 @@ def test_repeated_launches_are_bit_identical(fa8, cuda, B, H, S, D, causal):
     for _ in range(12):
         again = fa8.flash_attn_fp8_forward_ex(q, k, v, causal=causal)
         assert torch.equal(first, again)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_e4m3_extremes(fa8, cuda, D):
+    """Inputs at e4m3's largest magnitudes (+-448, the codes 0x7E / 0xFE) and rows
+    whose scores span far more than fp32's exponent range: the lazy rescale
+    must jump the running max without overflowing P, and O stays within V's range."""
+    import torch
+    rng = np.random.default_rng(3)
+    S = 512
+    q = ref.make_inputs((1, 2, S, D), "normal", 11)
+    k = ref.make_inputs((1, 2, S, D), "normal", 12)
+    v = ref.make_inputs((1, 2, D, S), "normal", 13)
+    # a few keys and query rows saturated at +-448, one key tile late in the order
+    for t in (q, k):
+        rows = rng.choice(S, 24, replace=False)
+        t[0, :, rows, :] = np.where(rng.random((2, 24, D)) < 0.5, 0x7E, 0xFE).transpose(1, 0, 2)
+    v[0, :, :, rng.choice(S, 16, replace=False)] = 0x7E
+    for causal in (False, True):
+        out = run_ex(fa8, q, k, v, cuda, causal=causal)
+        o_ref, _ = U.oracle(q, k, v, causal)
+        got = out.float().cpu().numpy()
+        assert np.isfinite(got).all()
+        # scores reach 448^2 * D: judge errors relative to V's scale (448)
+        err = np.abs(got - o_ref)
+        assert err.max() <= 448 * 0.0625 + U.MAX_ABS
+        assert err.mean() <= 448 * U.MEAN_ABS
+
+
+@pytest.mark.parametrize("Sq,Skv,D", [(256, 640, 128), (640, 256, 128), (384, 1024, 64),
+                                      (1000, 200, 64)])
+def test_causal_with_unequal_lengths(fa8, cuda, Sq, Skv, D):
+    """Causal mask key <= query in positions from 0 for both (no offsets),
+    with S_q != S_kv outside varlen: rows past S_kv see every key."""
+    q, k, v = U.inputs(1, 2, 2, Sq, Skv, D, "normal", seed=Sq * 3 + Skv)
+    out, lse = run_ex(fa8, q, k, v, cuda, causal=True, return_lse=True)
+    o_ref, l_ref = U.oracle(q, k, v, True)
+    U.assert_close(out.float().cpu().numpy(), o_ref)
+    l = lse.cpu().numpy()
+    fin = np.isfinite(l_ref)
+    assert np.array_equal(np.isfinite(l), fin)
+    assert np.abs(l[fin] - l_ref[fin]).max() < 1e-3
