@@ -531,6 +531,8 @@ def run_framework(args):
                "sample": f"{units} (batch, head) units of the workload (S={S}, D={D}, "
                          f"causal={causal}) in {el:.1f}s, test.py:8-15 math in fp32 numpy"}
 
+    aux = aux_kernel_lines(device) if rank == 0 and not args.no_aux else None
+
     c5 = None
     if world > 1 and not args.no_cp:
         c5 = run_c5_cp(args, world, rank, local, device, ranks)
@@ -570,6 +572,7 @@ def run_framework(args):
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "aux_kernels": aux,
             "c5_cp": c5,
         }
         print(json.dumps(line), flush=True)
@@ -577,6 +580,52 @@ def run_framework(args):
         import torch.distributed as dist
         dist.destroy_process_group()
     return 0
+
+
+def aux_kernel_lines(device):
+    """Device time and HBM fraction of the two kernels either side of the
+    forward, on the headline shape: the fp16 -> e4m3 quantiser (Q/K layout, and
+    V with the transpose to (B, H, D, S)) and the LSE merge of the context-
+    parallel path (four fp32 partials of (H=32, S=8192, D=128) rows, C5's
+    per-rank chunk). Inputs are larger than L2."""
+    import torch
+    import ada_cute_fp8_flash_attention_b200 as fa8
+    hbm, _, src = load_peaks()
+    W = CONFIGS["c2"]
+    B, H, S, D = W["batch"], W["heads"], W["seqlen"], W["head_dim"]
+    out = {}
+
+    def timed(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    x = torch.randn((B, H, S, D), device=device, dtype=torch.float16)
+    for name, tr in (("quantize_e4m3", False), ("quantize_e4m3_transpose", True)):
+        ms = timed(lambda: fa8.quantize_e4m3(x, 1.0, tr))
+        nbytes = x.numel() * 3  # 2 B read + 1 B written per element
+        out[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                     "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / hbm,
+                     "shape": f"fp16 (B{B} H{H} S{S} D{D})" + (" -> (B,H,D,S)" if tr else "")}
+    del x
+    rows, n = 32 * 8192, 4
+    parts = [torch.randn((rows, 128), device=device, dtype=torch.float32) for _ in range(n)]
+    lses = [torch.randn((rows,), device=device, dtype=torch.float32) for _ in range(n)]
+    ms = timed(lambda: fa8.lse_merge(parts, lses))
+    nbytes = n * rows * (128 * 4 + 4) + rows * (128 * 2 + 4)
+    out["lse_merge"] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                        "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / hbm,
+                        "shape": f"{n} fp32 parts of {rows} rows x 128 -> fp16"}
+    out["peak_gbs"] = hbm
+    out["peak_source"] = f"hbm_gbs of MEASURED_PEAKS.json ({src})"
+    return out
 
 
 def c5_chunk(cid, salt, shape, device, seed):
@@ -732,6 +781,7 @@ def main():
     ap.add_argument("--no-weak", action="store_true", help="skip the weak-scaling figure")
     ap.add_argument("--no-cp", action="store_true", help="skip the C5 context-parallel sub-line")
     ap.add_argument("--no-probe", action="store_true", help="skip the cuBLASLt FP8 GEMM probe")
+    ap.add_argument("--no-aux", action="store_true", help="skip the quantiser / merge timing")
     ap.add_argument("--cp-steps", type=int, default=4)
     ap.add_argument("--workload", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--cp-schedule", default="allgather", choices=["allgather", "ring"],
