@@ -26,6 +26,7 @@ __all__ = [
     "flash_attn_fp8_forward",
     "flash_attn_fp8_forward_ex",
     "flash_attn_fp8_varlen_forward",
+    "flash_attn_fp8_backward",
     "lse_merge",
     "quantize_e4m3",
     "launch_count",
@@ -101,6 +102,22 @@ def flash_attn_fp8_varlen_forward(q, k, v, cu_seqlens_q, cu_seqlens_kv, max_seql
                                            int(max_seqlen_q), causal, softmax_scale, v_layout,
                                            return_lse, out_dtype, status)
     return (res[0], res[1]) if return_lse else res[0]
+
+
+def flash_attn_fp8_backward(q, k, v, out, grad_out, lse, causal=True, softmax_scale=None,
+                            v_layout="bhds"):
+    """Gradients of the FP8 attention with respect to its e4m3 inputs.
+
+    q (B,H,S_q,D), k (B,H_kv,S_kv,D), v (B,H_kv,D,S_kv) for "bhds" or (B,H_kv,S_kv,D)
+    for "bhsd", all e4m3; ``out`` (fp16) and ``lse`` (fp32 (B,H,S_q)) as the forward
+    returned them (``return_lse=True``); ``grad_out`` fp16 like ``out``. P is
+    recomputed exactly in fp32. Returns (dq, dk, dv) in fp32; dk and dv are
+    (B, H_kv, S_kv, D) with the query heads of each K/V head summed. The
+    reference has no backward; this is the gradient of the same forward.
+    """
+    dq, dk, dv = _C.flash_attn_fp8_backward(q, k, v, out, grad_out, lse, causal, softmax_scale,
+                                            v_layout)
+    return dq, dk, dv
 
 
 def lse_merge(outs, lses):

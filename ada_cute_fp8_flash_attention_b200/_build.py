@@ -32,7 +32,7 @@ NVCC_FLAGS = [
     "-Xptxas", "-v",
 ]
 
-CUDA_SOURCES = ["fa8_api.cu", "fa8_aux.cu"]
+CUDA_SOURCES = ["fa8_api.cu", "fa8_aux.cu", "fa8_bwd.cu"]
 CUDA_HEADERS = ["fa8_fwd_kernel.cuh", "fa8_softmax.cuh", "sm100_ptx.cuh"]
 
 

@@ -372,6 +372,62 @@ torch::Tensor quantize_e4m3(torch::Tensor x, double scale, bool transpose_last2)
   return y;
 }
 
+// Backward: gradients for q, k, v (e4m3, contiguous after .contiguous()),
+// given the forward's fp16 out and fp32 lse and the fp16 grad_out. Returns
+// [dq, dk, dv] in fp32 (dk, dv with the K/V head count).
+std::vector<torch::Tensor> flash_attn_fp8_backward(torch::Tensor q, torch::Tensor k,
+                                                   torch::Tensor v, torch::Tensor out,
+                                                   torch::Tensor grad_out, torch::Tensor lse,
+                                                   bool causal, c10::optional<double> softmax_scale,
+                                                   std::string v_layout) {
+  for (auto* t : {&q, &k, &v})
+    TORCH_CHECK(t->device().is_cuda() && t->scalar_type() == at::ScalarType::Float8_e4m3fn &&
+                    t->dim() == 4,
+                "q, k, v must be 4-D CUDA float8_e4m3fn tensors");
+  TORCH_CHECK(v_layout == "bhds" || v_layout == "bhsd", "v_layout must be 'bhds' or 'bhsd'");
+  const int64_t B = q.size(0), H = q.size(1), Sq = q.size(2), D = q.size(3);
+  const int64_t Hkv = k.size(1), Skv = k.size(2);
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
+  TORCH_CHECK(k.size(0) == B && k.size(3) == D && Hkv > 0 && H % Hkv == 0,
+              "k must be (B, H_kv, S_kv, D) with H % H_kv == 0");
+  if (v_layout == "bhds") {
+    TORCH_CHECK(v.sizes() == torch::IntArrayRef({B, Hkv, D, Skv}), "v must be (B, H_kv, D, S_kv)");
+  } else {
+    TORCH_CHECK(v.sizes() == k.sizes(), "v must be (B, H_kv, S_kv, D)");
+  }
+  for (auto* t : {&out, &grad_out}) {
+    TORCH_CHECK(t->device() == q.device() && t->scalar_type() == at::ScalarType::Half &&
+                    t->sizes() == q.sizes(),
+                "out and grad_out must be fp16 (B, H, S_q, D) on q's device");
+  }
+  TORCH_CHECK(lse.device() == q.device() && lse.scalar_type() == at::ScalarType::Float &&
+                  lse.sizes() == torch::IntArrayRef({B, H, Sq}),
+              "lse must be float32 (B, H, S_q) on q's device");
+  TORCH_CHECK(k.device() == q.device() && v.device() == q.device(), "q, k, v on one device");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream(q.get_device());
+  q = q.contiguous(); k = k.contiguous(); v = v.contiguous();
+  out = out.contiguous(); grad_out = grad_out.contiguous(); lse = lse.contiguous();
+  auto f32 = q.options().dtype(at::ScalarType::Float);
+  auto dq = torch::empty({B, H, Sq, D}, f32);
+  auto dk = torch::empty({B, Hkv, Skv, D}, f32);
+  auto dv = torch::empty({B, Hkv, Skv, D}, f32);
+  fa8_bwd_params p;
+  fa8_bwd_params_init(&p, B, H, Hkv, Sq, Skv, D);
+  p.q = q.data_ptr(); p.k = k.data_ptr(); p.v = v.data_ptr();
+  p.o = out.data_ptr(); p.d_o = grad_out.data_ptr(); p.lse = lse.data_ptr<float>();
+  p.dq = dq.data_ptr<float>(); p.dk = dk.data_ptr<float>(); p.dv = dv.data_ptr<float>();
+  p.causal = causal ? 1 : 0;
+  p.softmax_scale = static_cast<float>(softmax_scale.has_value() ? *softmax_scale
+                                                                 : 1.0 / std::sqrt((double)D));
+  p.v_layout = v_layout == "bhsd" ? FA8_V_BHSD : FA8_V_BHDS;
+  const int64_t ws_bytes = fa8_bwd_workspace_size(&p);
+  TORCH_CHECK(ws_bytes >= 0, "fa8_bwd_workspace_size: ", fa8_last_error_message());
+  auto ws = torch::empty({std::max<int64_t>(ws_bytes, 1)}, q.options().dtype(at::kByte));
+  check_status(fa8_bwd(&p, ws.data_ptr(), ws_bytes, stream.stream()), "fa8_bwd");
+  return {dq, dk, dv};
+}
+
 int64_t launch_count() { return (int64_t)fa8_launch_count(); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -395,5 +451,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lse_merge", &lse_merge, "log-sum-exp merge of partial attention outputs");
   m.def("quantize_e4m3", &quantize_e4m3, py::arg("x"), py::arg("scale") = 1.0,
         py::arg("transpose_last2") = false, "fp16/bf16 -> e4m3 (optionally transposed)");
+  m.def("flash_attn_fp8_backward", &flash_attn_fp8_backward, py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("out"), py::arg("grad_out"), py::arg("lse"),
+        py::arg("causal") = true, py::arg("softmax_scale") = py::none(),
+        py::arg("v_layout") = "bhds", "gradients [dq, dk, dv] (fp32) of the FP8 attention");
   m.def("launch_count", &launch_count, "kernel launches issued by the C ABI so far");
 }

@@ -234,6 +234,40 @@ int fa8_quantize_e4m3(const void* x, int in_dtype, void* y, int64_t batch,
 
 /* Human-readable text for an fa8_status, plus the last CUDA error seen by
  * this thread when the status is FA8_ERR_CUDA. */
+/*
+ * Backward pass: gradients of O = softmax(scale * Q K^T [causal]) V with
+ * respect to the e4m3 Q, K and V that fa8_fwd consumed. No counterpart in
+ * the reference, which has no backward. Inputs: q, k (contiguous
+ * [b][h][s][d] / [b][h_kv][s][d] e4m3), v (contiguous, v_layout), o and d_o
+ * (contiguous fp16 [b][h][s_q][d], o as fa8_fwd wrote it), lse (contiguous
+ * fp32 [b][h][s_q], natural log, as fa8_fwd wrote it). Outputs (fp32,
+ * contiguous): dq [b][h][s_q][d], dk and dv [b][h_kv][s_kv][d] (GQA heads
+ * summed). Causal masking is key <= query (no offsets). The caller provides
+ * fa8_bwd_workspace_size() bytes of device workspace, 256-byte aligned.
+ */
+typedef struct fa8_bwd_params {
+  int64_t batch, heads, heads_kv, seqlen_q, seqlen_kv, head_dim;
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* d_o;
+  const float* lse;
+  float* dq;
+  float* dk;
+  float* dv;
+  int causal;             /* default 1                                    */
+  float softmax_scale;    /* <= 0: 1/sqrt(head_dim)                       */
+  int v_layout;           /* FA8_V_BHDS (default) or FA8_V_BHSD           */
+  int* status;            /* optional device word, FA8_DEVERR_* bits      */
+  long long timeout_cycles; /* bound of every wait; <= 0: ~2 s            */
+} fa8_bwd_params;
+
+void fa8_bwd_params_init(fa8_bwd_params* p, int64_t batch, int64_t heads, int64_t heads_kv,
+                         int64_t seqlen_q, int64_t seqlen_kv, int64_t head_dim);
+int64_t fa8_bwd_workspace_size(const fa8_bwd_params* p);
+int fa8_bwd(const fa8_bwd_params* p, void* workspace, int64_t workspace_bytes, void* stream);
+
 const char* fa8_status_string(int status);
 const char* fa8_last_error_message(void);
 

@@ -47,6 +47,7 @@ __all__ = [
     "e4m3_encode",
     "attention",
     "reference_kernel_semantics",
+    "attention_backward",
     "make_inputs",
 ]
 
@@ -130,6 +131,50 @@ def attention(q, k, v_bhds, causal: bool, scale: float | None = None,
             lse[b, h] = np.where(l[:, 0] > 0, np.log(np.where(l[:, 0] > 0, l[:, 0], 1.0)) + m_safe[:, 0],
                                  -np.inf)
     return o, lse
+
+
+def attention_backward(q, k, v_bhds, o, d_o, lse, causal: bool, scale: float | None = None):
+    """float64 gradients of ``attention`` (the reference has no backward).
+
+    Restates the standard softmax-attention gradient as a function of the
+    forward's outputs, exactly as the kernel evaluates it: P = exp(scale*q k^T
+    - lse) (masked keys 0), dV = P^T dO, dP = dO V^T, Delta = rowsum(dO * o),
+    dS = P * (dP - Delta), dQ = scale dS K, dK = scale dS^T Q. Shapes as in
+    ``attention`` plus o, d_o (B,H,Sq,D) and lse (B,H,Sq). Returns dq
+    (B,H,Sq,D), dk and dv (B,Hkv,Skv,D) with the query heads of each K/V head
+    summed (GQA).
+    """
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.swapaxes(np.asarray(v_bhds, np.float64), 2, 3)
+    o = np.asarray(o, np.float64)
+    d_o = np.asarray(d_o, np.float64)
+    lse = np.asarray(lse, np.float64)
+    B, H, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    g = H // Hkv
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dq = np.zeros_like(q)
+    dk = np.zeros((B, Hkv, Skv, D))
+    dv = np.zeros((B, Hkv, Skv, D))
+    mask = (np.arange(Skv)[None, :] <= np.arange(Sq)[:, None]) if causal else None
+    for b in range(B):
+        for h in range(H):
+            kh, vh = k[b, h // g], v[b, h // g]
+            s = q[b, h] @ kh.T * scale
+            with np.errstate(invalid="ignore", over="ignore"):
+                p = np.exp(s - lse[b, h][:, None])
+            p = np.where(np.isfinite(lse[b, h])[:, None], p, 0.0)
+            if causal:
+                p = np.where(mask, p, 0.0)
+            dv[b, h // g] += p.T @ d_o[b, h]
+            dp = d_o[b, h] @ vh.T
+            delta = (d_o[b, h] * o[b, h]).sum(axis=1)
+            ds = p * (dp - delta[:, None])
+            dq[b, h] = scale * ds @ kh
+            dk[b, h // g] += scale * ds.T @ q[b, h]
+    return dq, dk, dv
 
 
 def reference_kernel_semantics(q, k, v_bhds, tile: int = 64):
