@@ -13,6 +13,8 @@
  *                     csrc/flash_attention.cu:487-506 (launcher),
  *                     csrc/flash.h:11-26 (Flash_fwd_params),
  *                     bound at csrc/attention_api.cpp:6-9.
+ *   fa8_bwd        <- no counterpart in the reference (forward only); the
+ *                     gradient of the same attention for training callers.
  *   fa8_lse_merge  <- no counterpart in the reference (which emits no LSE);
  *                     merges partial outputs of the context-parallel ring.
  *   fa8_quantize_e4m3 <- the torch casts that prepare the kernel inputs in
