@@ -12,17 +12,19 @@
 //
 // Three launches:
 //   1. bwd_prep_kernel: e4m3 -> fp16 copies of Q, K, V (exact: every e4m3 value
-//      is an fp16 value) in the row layout [s][d] and, where a product needs
-//      it as a K-major B operand, the transposed layout [d][s]; dO^T likewise;
-//      sequence padded to a multiple of 128 with zeros.
+//      is an fp16 value) in the row layout [s][d], sequence padded to a
+//      multiple of 128 with zeros. Products that need a tile transposed read
+//      the same copy as an MN-major operand.
 //   2. bwd_delta_kernel: Delta = rowsum(dO * O) in fp32.
 //   3. bwd_dkdv_kernel (one CTA per 128-key tile and KV head): for each query
-//      tile, S^T = K Q^T and dP^T = V dO^T into TMEM (tcgen05, f16 x f16 -> f32),
-//      P^T and dS^T in fp16 to shared memory by one thread per key, then
-//      dV += P^T dO and dK += dS^T Q accumulate in TMEM.
+//      tile, S^T = K Q^T and dP^T = V dO^T into TMEM (tcgen05, f16 x f16 -> f32);
+//      16 warps (4 per TMEM lane quarter, 32 query columns each) turn them
+//      into fp16 P^T and dS^T written back into TMEM; dV += P^T dO and
+//      dK += dS^T Q then read A from TMEM and accumulate in TMEM.
 //   4. bwd_dq_kernel (one CTA per 128-query tile and head): for each key tile,
-//      S = Q K^T and dP = dO V^T, dS in fp16, dQ += dS K in TMEM.
-// Every operand moves by TMA into 128B-swizzled 64-column panels; one thread
+//      S = Q K^T and dP = dO V^T, dS in fp16 (TMEM), dQ += dS K in TMEM.
+// Operands move by TMA into 128B-swizzled 64-column panels, the next
+// iteration's tiles into a second buffer while this one computes; one thread
 // issues the tcgen05 products; every wait is bounded and reports a timeout in
 // the status word instead of hanging.
 #include <cuda.h>
@@ -70,18 +72,27 @@ __device__ __forceinline__ uint64_t desc_k(uint32_t base, int kk, int panel_byte
   return ptx::smem_desc_kmajor(base + (uint32_t)((kk >> 2) * panel_bytes + (kk & 3) * 32), 128);
 }
 
+// Descriptor of K step kk (16 rows of 128 B) of an MN-major operand stored as
+// [K rows][64-column] panels, 128B swizzled as TMA writes a [rows][D] tile:
+// 64-column atoms along MN are `lbo` bytes apart (the panel size), 8-row groups
+// along K 1024 bytes apart.
+__device__ __forceinline__ uint64_t desc_mn(uint32_t base, int kk, uint32_t lbo) {
+  const uint32_t saddr = base + (uint32_t)kk * 2048u;
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, long long limit) {
   const long long t0 = clock64();
   while (!ptx::mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > limit) return false;
   }
   return true;
-}
-
-// Row r of a thread-written 128-column fp16 tile (two 64-column panels,
-// 128B swizzle): 16-byte chunk c (8 halves, columns 8c..8c+7).
-__device__ __forceinline__ uint32_t chunk_addr(uint32_t tile, int r, int c) {
-  return tile + (uint32_t)((c >> 3) * kPanelBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -167,42 +178,68 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(const __half* d_o, const
   if (lane == 0) delta[w] = acc;
 }
 
+// ------------------------------------------------------------------ shared parts
+constexpr int kThreadsBwd = 512;  // 16 warps: warp w reads TMEM lanes 32 (w % 4) .. +31
+                                  // and key / query columns 32 (w / 4) .. +31
+
+// Warp-collective store of 16 consecutive 32-bit TMEM columns (one per register).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]: A is M = 128 lanes x K = 16 halves packed two
+// per 32-bit column (8 columns).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// TMEM column of K step kk of a 128-wide fp16 operand that the elementwise
+// pass wrote as 16-column blocks at the start of each 32-column chunk.
+__device__ __forceinline__ uint32_t ts_col(int kk) { return 32u * (kk >> 1) + 8u * (kk & 1); }
+
 // ------------------------------------------------------------------ dK, dV
 template <int D>
 struct DkdvCfg {
   static constexpr int kRowTile = kTile * D * 2;     // [128][D] fp16 (D / 64 panels)
-  static constexpr int kTPanel = D * 128;            // [D][64] fp16 panel of a transposed tile
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kRowTile;
-  static constexpr int kOffQ = kOffV + kRowTile;     // Q_i, then Q_i^T (same size)
-  static constexpr int kOffDo = kOffQ + kRowTile;    // dO_i, then dO_i^T
-  static constexpr int kOffP = kOffDo + kRowTile;    // P^T [128 keys][128 queries]
-  static constexpr int kOffDs = kOffP + 2 * kPanelBytes;
-  static constexpr int kOffLse = kOffDs + 2 * kPanelBytes;  // 128 floats: LSE * log2(e)
+  static constexpr int kOffQ = kOffV + kRowTile;     // two buffers: Q_i, Q_i+1
+  static constexpr int kOffDo = kOffQ + 2 * kRowTile;  // two buffers: dO_i, dO_i+1
+  static constexpr int kOffLse = kOffDo + 2 * kRowTile;  // 128 floats: LSE * log2(e)
   static constexpr int kOffDelta = kOffLse + 512;
   static constexpr int kSmem = kOffDelta + 512;
   static constexpr int kSmemAlloc = kSmem + 1024;
-  // TMEM: S^T | dP^T | dV | dK
+  // TMEM: S^T (then P^T) | dP^T (then dS^T) | dV | dK
   static constexpr uint32_t kColS = 0, kColDp = 128, kColDv = 256, kColDk = 256 + D;
-  static_assert(2 * kTPanel == kRowTile, "a transposed tile fills a row tile's buffer");
 };
 
 template <int D>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kThreadsBwd, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                    const __grid_constant__ CUtensorMap tm_qt,
-                    const __grid_constant__ CUtensorMap tm_dot, const Params p) {
+                    const Params p) {
   using C = DkdvCfg<D>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_ld, bar_ld2, bar_mma;
+  __shared__ uint64_t bar_ld[2], bar_mma;
   __shared__ uint32_t tmem_sh;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sb = ptx::smem_u32(smem);
   float* lse_sh = reinterpret_cast<float*>(smem + C::kOffLse);
   float* delta_sh = reinterpret_cast<float*>(smem + C::kOffDelta);
-  const int r = threadIdx.x, warp = r / 32;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int quad = warp & 3, chunk = warp >> 2;
+  const int r = quad * 32 + lane;  // key row of the tile == TMEM lane
   const int j = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int key = j * kTile + r;
   const int nq = (p.sq + kTile - 1) / kTile;
@@ -210,9 +247,9 @@ __global__ void __launch_bounds__(128, 1)
   const int n_heads = p.group;
   const int n_iter = (i_lo < nq ? nq - i_lo : 0) * n_heads;
 
-  if (r == 0) {
-    ptx::mbar_init(&bar_ld, 1);
-    ptx::mbar_init(&bar_ld2, 1);
+  if (tid == 0) {
+    ptx::mbar_init(&bar_ld[0], 1);
+    ptx::mbar_init(&bar_ld[1], 1);
     ptx::mbar_init(&bar_mma, 1);
     ptx::fence_mbar_init();
   }
@@ -224,54 +261,62 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = tmem_sh;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
   constexpr uint32_t idesc_s = idesc_f16_f32(128, 128);
-  constexpr uint32_t idesc_g = idesc_f16_f32(128, D);
-  uint32_t ph_ld = 0, ph_ld2 = 0, ph_mma = 0;
+  constexpr uint32_t idesc_g = ptx::idesc_e4m3_f32(128, D, true);  // B MN-major
+  uint32_t ph_mma = 0;
   bool ok = true;
+
+  // Q_i and dO_i of iteration `it` into buffer it & 1 (K_j, V_j with the first).
+  auto issue_loads = [&](int it) {
+    const int i = i_lo + it / n_heads;
+    const int h = hk * p.group + it % n_heads;
+    const int buf = it & 1;
+    uint32_t bytes = 2 * C::kRowTile;
+    if (it == 0) bytes += 2 * C::kRowTile;
+    ptx::mbar_arrive_expect_tx(&bar_ld[buf], bytes);
+    const uint64_t pol = ptx::policy_evict_last();
+#pragma unroll
+    for (int pnl = 0; pnl < D / 64; ++pnl) {
+      if (it == 0) {
+        ptx::tma_load_4d(smem + C::kOffK + pnl * kPanelBytes, &tm_k, &bar_ld[buf], pnl * 64, j * kTile, hk, b, pol);
+        ptx::tma_load_4d(smem + C::kOffV + pnl * kPanelBytes, &tm_v, &bar_ld[buf], pnl * 64, j * kTile, hk, b, pol);
+      }
+      ptx::tma_load_4d(smem + C::kOffQ + buf * C::kRowTile + pnl * kPanelBytes, &tm_q, &bar_ld[buf],
+                       pnl * 64, i * kTile, h, b, pol);
+      ptx::tma_load_4d(smem + C::kOffDo + buf * C::kRowTile + pnl * kPanelBytes, &tm_do, &bar_ld[buf],
+                       pnl * 64, i * kTile, h, b, pol);
+    }
+  };
+  if (tid == 0 && n_iter > 0) issue_loads(0);
 
   for (int it = 0; it < n_iter && ok; ++it) {
     const int i = i_lo + it / n_heads;
     const int h = hk * p.group + it % n_heads;
-    // 1. loads: Q_i, dO_i (+ K_j, V_j once); LSE and Delta of the query tile
-    if (r == 0) {
-      uint32_t bytes = 2 * C::kRowTile;
-      if (it == 0) bytes += 2 * C::kRowTile;
-      ptx::mbar_arrive_expect_tx(&bar_ld, bytes);
-      const uint64_t pol = ptx::policy_evict_last();
-      if (it == 0) {
-#pragma unroll
-        for (int pnl = 0; pnl < D / 64; ++pnl) {
-          ptx::tma_load_4d(smem + C::kOffK + pnl * kPanelBytes, &tm_k, &bar_ld, pnl * 64, j * kTile, hk, b, pol);
-          ptx::tma_load_4d(smem + C::kOffV + pnl * kPanelBytes, &tm_v, &bar_ld, pnl * 64, j * kTile, hk, b, pol);
-        }
-      }
-#pragma unroll
-      for (int pnl = 0; pnl < D / 64; ++pnl) {
-        ptx::tma_load_4d(smem + C::kOffQ + pnl * kPanelBytes, &tm_q, &bar_ld, pnl * 64, i * kTile, h, b, pol);
-        ptx::tma_load_4d(smem + C::kOffDo + pnl * kPanelBytes, &tm_do, &bar_ld, pnl * 64, i * kTile, h, b, pol);
-      }
-    }
-    {
-      const int q = i * kTile + r;
+    const int buf = it & 1;
+    // The other buffer was last read by the products of iteration it - 1 (complete).
+    if (tid == 0 && it + 1 < n_iter) issue_loads(it + 1);
+    if (tid < kTile) {
+      const int q = i * kTile + tid;
       const long long row = ((long long)b * p.heads + h);
       const float l = q < p.sq ? p.lse[row * p.sq + q] : INFINITY;
-      lse_sh[r] = (l == -INFINITY) ? INFINITY : l * 1.4426950408889634f;
-      delta_sh[r] = p.delta[row * p.sqp + i * kTile + r];
+      lse_sh[tid] = (l == -INFINITY) ? INFINITY : l * 1.4426950408889634f;
+      delta_sh[tid] = p.delta[row * p.sqp + i * kTile + tid];
     }
-    ok = wait_bar(&bar_ld, ph_ld, p.timeout);
-    ph_ld ^= 1;
+    ok = wait_bar(&bar_ld[buf], (uint32_t)(it >> 1) & 1u, p.timeout);
     ok = __syncthreads_and(ok);
     if (!ok) break;
-    // 2. S^T = K Q^T, dP^T = V dO^T
-    if (r == 0) {
+    const uint32_t q_addr = sb + C::kOffQ + buf * C::kRowTile;
+    const uint32_t do_addr = sb + C::kOffDo + buf * C::kRowTile;
+    // S^T = K Q^T, dP^T = V dO^T
+    if (tid == 0) {
       ptx::tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         umma_f16(tmem + C::kColS, desc_k(sb + C::kOffK, kk, kPanelBytes),
-                 desc_k(sb + C::kOffQ, kk, kPanelBytes), idesc_s, kk > 0);
+                 desc_k(q_addr, kk, kPanelBytes), idesc_s, kk > 0);
         umma_f16(tmem + C::kColDp, desc_k(sb + C::kOffV, kk, kPanelBytes),
-                 desc_k(sb + C::kOffDo, kk, kPanelBytes), idesc_s, kk > 0);
+                 desc_k(do_addr, kk, kPanelBytes), idesc_s, kk > 0);
       }
       ptx::umma_commit(&bar_mma);
     }
@@ -279,65 +324,50 @@ __global__ void __launch_bounds__(128, 1)
     ph_mma ^= 1;
     ok = __syncthreads_and(ok);
     if (!ok) break;
-    // 3. Q_i^T and dO_i^T replace Q_i and dO_i (the products above have read them)
-    if (r == 0) {
-      ptx::mbar_arrive_expect_tx(&bar_ld2, 2 * C::kRowTile);
-      const uint64_t pol = ptx::policy_evict_first();
-#pragma unroll
-      for (int pnl = 0; pnl < 2; ++pnl) {
-        ptx::tma_load_4d(smem + C::kOffQ + pnl * C::kTPanel, &tm_qt, &bar_ld2, i * kTile + pnl * 64, 0, h, b, pol);
-        ptx::tma_load_4d(smem + C::kOffDo + pnl * C::kTPanel, &tm_dot, &bar_ld2, i * kTile + pnl * 64, 0, h, b, pol);
-      }
-    }
-    // 4. P^T and dS^T rows (this thread's key) in fp16
+    // P^T and dS^T of this warp's 32 queries, fp16, back into the first 16
+    // columns of the chunk they were read from.
     ptx::tc_fence_after();
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    {
       uint32_t us[32], ud[32];
-      ptx::tmem_ld32(tmem + lane_off + C::kColS + c * 32, us);
-      ptx::tmem_ld32(tmem + lane_off + C::kColDp + c * 32, ud);
+      ptx::tmem_ld32(tmem + lane_off + C::kColS + chunk * 32, us);
+      ptx::tmem_ld32(tmem + lane_off + C::kColDp + chunk * 32, ud);
       ptx::tmem_wait_ld();
       ptx::reg_fence32(us);
       ptx::reg_fence32(ud);
+      const int q0 = i * kTile + chunk * 32;
+      const bool full = key < p.skv && q0 + 31 < p.sq && (!p.causal || key <= q0);
       uint32_t hp[16], hd[16];
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
         float pv[2], dv[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const int qc = c * 32 + e + u;
-          const int q = i * kTile + qc;
-          const bool valid = key < p.skv && q < p.sq && (!p.causal || key <= q);
-          const float pr = valid ? exp2f(__uint_as_float(us[e + u]) * p.sl2 - lse_sh[qc]) : 0.f;
+          const int qc = chunk * 32 + e + u;
+          const int q = q0 + e + u;
+          const bool valid = full || (key < p.skv && q < p.sq && (!p.causal || key <= q));
+          const float pr = valid ? ptx::ex2(__uint_as_float(us[e + u]) * p.sl2 - lse_sh[qc]) : 0.f;
           pv[u] = pr;
           dv[u] = pr * (__uint_as_float(ud[e + u]) - delta_sh[qc]);
         }
         hp[e / 2] = pack_h2(pv[0], pv[1]);
         hd[e / 2] = pack_h2(dv[0], dv[1]);
       }
-#pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) {
-        ptx::st_shared_v4(chunk_addr(sb + C::kOffP, r, c * 4 + q8), hp[4 * q8], hp[4 * q8 + 1],
-                          hp[4 * q8 + 2], hp[4 * q8 + 3]);
-        ptx::st_shared_v4(chunk_addr(sb + C::kOffDs, r, c * 4 + q8), hd[4 * q8], hd[4 * q8 + 1],
-                          hd[4 * q8 + 2], hd[4 * q8 + 3]);
-      }
+      tmem_st16(tmem + lane_off + C::kColS + chunk * 32, hp);
+      tmem_st16(tmem + lane_off + C::kColDp + chunk * 32, hd);
+      ptx::tmem_wait_st();
     }
-    ptx::fence_proxy_async_smem();
     ptx::tc_fence_before();
-    ok = wait_bar(&bar_ld2, ph_ld2, p.timeout);
-    ph_ld2 ^= 1;
     ok = __syncthreads_and(ok);
     if (!ok) break;
-    // 5. dV += P^T dO, dK += dS^T Q (K = the 128 queries of the tile)
-    if (r == 0) {
+    // dV += P^T dO, dK += dS^T Q (K = the 128 queries of the tile)
+    if (tid == 0) {
       ptx::tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk) {
-        umma_f16(tmem + C::kColDv, desc_k(sb + C::kOffP, kk, kPanelBytes),
-                 desc_k(sb + C::kOffDo, kk, C::kTPanel), idesc_g, (it > 0 || kk > 0));
-        umma_f16(tmem + C::kColDk, desc_k(sb + C::kOffDs, kk, kPanelBytes),
-                 desc_k(sb + C::kOffQ, kk, C::kTPanel), idesc_g, (it > 0 || kk > 0));
+        umma_f16_ts(tmem + C::kColDv, tmem + C::kColS + ts_col(kk),
+                    desc_mn(do_addr, kk, kPanelBytes), idesc_g, (it > 0 || kk > 0));
+        umma_f16_ts(tmem + C::kColDk, tmem + C::kColDp + ts_col(kk),
+                    desc_mn(q_addr, kk, kPanelBytes), idesc_g, (it > 0 || kk > 0));
       }
       ptx::umma_commit(&bar_mma);
     }
@@ -345,41 +375,36 @@ __global__ void __launch_bounds__(128, 1)
     ph_mma ^= 1;
     ok = __syncthreads_and(ok);
   }
-  if (!ok) {
-    if (r == 0 && p.status) atomicOr(p.status, FA8_DEVERR_TIMEOUT);
+  if (!ok && tid == 0) {
+    if (p.status) atomicOr(p.status, FA8_DEVERR_TIMEOUT);
     // Let copies and products in flight finish (bounded) before TMEM is freed.
-    if (r == 0) {
-      wait_bar(&bar_ld, ph_ld, p.timeout);
-      wait_bar(&bar_ld2, ph_ld2, p.timeout);
-      wait_bar(&bar_mma, ph_mma, p.timeout);
-    }
+    wait_bar(&bar_ld[0], 0, p.timeout);
+    wait_bar(&bar_mma, ph_mma, p.timeout);
   }
+  __syncthreads();
   // Epilogue: dV and scale * dK rows of this key tile (zero when no query sees them).
   ptx::tc_fence_after();
-  {
+  if (chunk < D / 32) {
     const bool have = ok && n_iter > 0;
-    const long long row_off = (((long long)b * p.heads_kv + hk) * p.skv + key) * D;
-#pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t uv[32], uk[32];
-      ptx::tmem_ld32(tmem + lane_off + C::kColDv + c * 32, uv);
-      ptx::tmem_ld32(tmem + lane_off + C::kColDk + c * 32, uk);
-      ptx::tmem_wait_ld();
-      ptx::reg_fence32(uv);
-      ptx::reg_fence32(uk);
-      if (key < p.skv) {
+    const long long row_off = (((long long)b * p.heads_kv + hk) * p.skv + key) * D + chunk * 32;
+    uint32_t uv[32], uk[32];
+    ptx::tmem_ld32(tmem + lane_off + C::kColDv + chunk * 32, uv);
+    ptx::tmem_ld32(tmem + lane_off + C::kColDk + chunk * 32, uk);
+    ptx::tmem_wait_ld();
+    ptx::reg_fence32(uv);
+    ptx::reg_fence32(uk);
+    if (key < p.skv) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          const float4 a = have ? make_float4(__uint_as_float(uv[e]), __uint_as_float(uv[e + 1]),
-                                              __uint_as_float(uv[e + 2]), __uint_as_float(uv[e + 3]))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float4 k4 =
-              have ? make_float4(__uint_as_float(uk[e]) * p.scale, __uint_as_float(uk[e + 1]) * p.scale,
-                                 __uint_as_float(uk[e + 2]) * p.scale, __uint_as_float(uk[e + 3]) * p.scale)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4*>(p.dv + row_off + c * 32 + e) = a;
-          *reinterpret_cast<float4*>(p.dk + row_off + c * 32 + e) = k4;
-        }
+      for (int e = 0; e < 32; e += 4) {
+        const float4 a = have ? make_float4(__uint_as_float(uv[e]), __uint_as_float(uv[e + 1]),
+                                            __uint_as_float(uv[e + 2]), __uint_as_float(uv[e + 3]))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 k4 =
+            have ? make_float4(__uint_as_float(uk[e]) * p.scale, __uint_as_float(uk[e + 1]) * p.scale,
+                               __uint_as_float(uk[e + 2]) * p.scale, __uint_as_float(uk[e + 3]) * p.scale)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(p.dv + row_off + e) = a;
+        *reinterpret_cast<float4*>(p.dk + row_off + e) = k4;
       }
     }
   }
@@ -395,30 +420,31 @@ __global__ void __launch_bounds__(128, 1)
 template <int D>
 struct DqCfg {
   static constexpr int kRowTile = kTile * D * 2;
-  static constexpr int kTPanel = D * 128;
   static constexpr int kOffQ = 0;
   static constexpr int kOffDo = kOffQ + kRowTile;
-  static constexpr int kOffK = kOffDo + kRowTile;    // K_j, then K_j^T
-  static constexpr int kOffV = kOffK + kRowTile;
-  static constexpr int kOffDs = kOffV + kRowTile;    // dS [128 queries][128 keys]
-  static constexpr int kSmem = kOffDs + 2 * kPanelBytes;
+  static constexpr int kOffK = kOffDo + kRowTile;    // two buffers: K_j, K_j+1
+  static constexpr int kOffV = kOffK + 2 * kRowTile;  // two buffers: V_j, V_j+1
+  static constexpr int kSmem = kOffV + 2 * kRowTile;
   static constexpr int kSmemAlloc = kSmem + 1024;
+  // TMEM: S | dP (then dS) | dQ
   static constexpr uint32_t kColS = 0, kColDp = 128, kColDq = 256;
 };
 
 template <int D>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kThreadsBwd, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                  const __grid_constant__ CUtensorMap tm_kt, const Params p) {
+                  const Params p) {
   using C = DqCfg<D>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_ld, bar_ld2, bar_mma;
+  __shared__ uint64_t bar_ld[2], bar_mma;
   __shared__ uint32_t tmem_sh;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sb = ptx::smem_u32(smem);
-  const int r = threadIdx.x, warp = r / 32;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int quad = warp & 3, chunk = warp >> 2;
+  const int r = quad * 32 + lane;  // query row of the tile == TMEM lane
   const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.group;
   const int q = i * kTile + r;
@@ -432,9 +458,9 @@ __global__ void __launch_bounds__(128, 1)
     delta = p.delta[row * p.sqp + q];
   }
 
-  if (r == 0) {
-    ptx::mbar_init(&bar_ld, 1);
-    ptx::mbar_init(&bar_ld2, 1);
+  if (tid == 0) {
+    ptx::mbar_init(&bar_ld[0], 1);
+    ptx::mbar_init(&bar_ld[1], 1);
     ptx::mbar_init(&bar_mma, 1);
     ptx::fence_mbar_init();
   }
@@ -446,40 +472,48 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = tmem_sh;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
   constexpr uint32_t idesc_s = idesc_f16_f32(128, 128);
-  constexpr uint32_t idesc_g = idesc_f16_f32(128, D);
-  uint32_t ph_ld = 0, ph_ld2 = 0, ph_mma = 0;
+  constexpr uint32_t idesc_g = ptx::idesc_e4m3_f32(128, D, true);  // B MN-major
+  uint32_t ph_mma = 0;
   bool ok = true;
 
-  for (int j = 0; j < n_iter && ok; ++j) {
-    if (r == 0) {
-      uint32_t bytes = 2 * C::kRowTile;
-      if (j == 0) bytes += 2 * C::kRowTile;
-      ptx::mbar_arrive_expect_tx(&bar_ld, bytes);
-      const uint64_t pol = ptx::policy_evict_last();
+  auto issue_loads = [&](int jj) {
+    const int buf = jj & 1;
+    uint32_t bytes = 2 * C::kRowTile;
+    if (jj == 0) bytes += 2 * C::kRowTile;
+    ptx::mbar_arrive_expect_tx(&bar_ld[buf], bytes);
+    const uint64_t pol = ptx::policy_evict_last();
 #pragma unroll
-      for (int pnl = 0; pnl < D / 64; ++pnl) {
-        if (j == 0) {
-          ptx::tma_load_4d(smem + C::kOffQ + pnl * kPanelBytes, &tm_q, &bar_ld, pnl * 64, i * kTile, h, b, pol);
-          ptx::tma_load_4d(smem + C::kOffDo + pnl * kPanelBytes, &tm_do, &bar_ld, pnl * 64, i * kTile, h, b, pol);
-        }
-        ptx::tma_load_4d(smem + C::kOffK + pnl * kPanelBytes, &tm_k, &bar_ld, pnl * 64, j * kTile, hk, b, pol);
-        ptx::tma_load_4d(smem + C::kOffV + pnl * kPanelBytes, &tm_v, &bar_ld, pnl * 64, j * kTile, hk, b, pol);
+    for (int pnl = 0; pnl < D / 64; ++pnl) {
+      if (jj == 0) {
+        ptx::tma_load_4d(smem + C::kOffQ + pnl * kPanelBytes, &tm_q, &bar_ld[buf], pnl * 64, i * kTile, h, b, pol);
+        ptx::tma_load_4d(smem + C::kOffDo + pnl * kPanelBytes, &tm_do, &bar_ld[buf], pnl * 64, i * kTile, h, b, pol);
       }
+      ptx::tma_load_4d(smem + C::kOffK + buf * C::kRowTile + pnl * kPanelBytes, &tm_k, &bar_ld[buf],
+                       pnl * 64, jj * kTile, hk, b, pol);
+      ptx::tma_load_4d(smem + C::kOffV + buf * C::kRowTile + pnl * kPanelBytes, &tm_v, &bar_ld[buf],
+                       pnl * 64, jj * kTile, hk, b, pol);
     }
-    ok = wait_bar(&bar_ld, ph_ld, p.timeout);
-    ph_ld ^= 1;
+  };
+  if (tid == 0 && n_iter > 0) issue_loads(0);
+
+  for (int j = 0; j < n_iter && ok; ++j) {
+    const int buf = j & 1;
+    if (tid == 0 && j + 1 < n_iter) issue_loads(j + 1);
+    ok = wait_bar(&bar_ld[buf], (uint32_t)(j >> 1) & 1u, p.timeout);
     ok = __syncthreads_and(ok);
     if (!ok) break;
-    if (r == 0) {
+    const uint32_t k_addr = sb + C::kOffK + buf * C::kRowTile;
+    const uint32_t v_addr = sb + C::kOffV + buf * C::kRowTile;
+    if (tid == 0) {
       ptx::tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         umma_f16(tmem + C::kColS, desc_k(sb + C::kOffQ, kk, kPanelBytes),
-                 desc_k(sb + C::kOffK, kk, kPanelBytes), idesc_s, kk > 0);
+                 desc_k(k_addr, kk, kPanelBytes), idesc_s, kk > 0);
         umma_f16(tmem + C::kColDp, desc_k(sb + C::kOffDo, kk, kPanelBytes),
-                 desc_k(sb + C::kOffV, kk, kPanelBytes), idesc_s, kk > 0);
+                 desc_k(v_addr, kk, kPanelBytes), idesc_s, kk > 0);
       }
       ptx::umma_commit(&bar_mma);
     }
@@ -487,76 +521,62 @@ __global__ void __launch_bounds__(128, 1)
     ph_mma ^= 1;
     ok = __syncthreads_and(ok);
     if (!ok) break;
-    if (r == 0) {
-      ptx::mbar_arrive_expect_tx(&bar_ld2, C::kRowTile);
-      const uint64_t pol = ptx::policy_evict_last();
-#pragma unroll
-      for (int pnl = 0; pnl < 2; ++pnl)
-        ptx::tma_load_4d(smem + C::kOffK + pnl * C::kTPanel, &tm_kt, &bar_ld2, j * kTile + pnl * 64, 0, hk, b, pol);
-    }
     ptx::tc_fence_after();
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    {
       uint32_t us[32], ud[32];
-      ptx::tmem_ld32(tmem + lane_off + C::kColS + c * 32, us);
-      ptx::tmem_ld32(tmem + lane_off + C::kColDp + c * 32, ud);
+      ptx::tmem_ld32(tmem + lane_off + C::kColS + chunk * 32, us);
+      ptx::tmem_ld32(tmem + lane_off + C::kColDp + chunk * 32, ud);
       ptx::tmem_wait_ld();
       ptx::reg_fence32(us);
       ptx::reg_fence32(ud);
+      const int k0 = j * kTile + chunk * 32;
+      const bool full = q < p.sq && k0 + 31 < p.skv && (!p.causal || k0 + 31 <= q);
       uint32_t hd[16];
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
         float dv[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const int key = j * kTile + c * 32 + e + u;
-          const bool valid = key < p.skv && q < p.sq && (!p.causal || key <= q);
-          const float pr = valid ? exp2f(__uint_as_float(us[e + u]) * p.sl2 - lse2) : 0.f;
+          const int key = k0 + e + u;
+          const bool valid = full || (key < p.skv && q < p.sq && (!p.causal || key <= q));
+          const float pr = valid ? ptx::ex2(__uint_as_float(us[e + u]) * p.sl2 - lse2) : 0.f;
           dv[u] = pr * (__uint_as_float(ud[e + u]) - delta);
         }
         hd[e / 2] = pack_h2(dv[0], dv[1]);
       }
-#pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8)
-        ptx::st_shared_v4(chunk_addr(sb + C::kOffDs, r, c * 4 + q8), hd[4 * q8], hd[4 * q8 + 1],
-                          hd[4 * q8 + 2], hd[4 * q8 + 3]);
+      tmem_st16(tmem + lane_off + C::kColDp + chunk * 32, hd);
+      ptx::tmem_wait_st();
     }
-    ptx::fence_proxy_async_smem();
     ptx::tc_fence_before();
-    ok = wait_bar(&bar_ld2, ph_ld2, p.timeout);
-    ph_ld2 ^= 1;
     ok = __syncthreads_and(ok);
     if (!ok) break;
-    if (r == 0) {
+    if (tid == 0) {
       ptx::tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk)
-        umma_f16(tmem + C::kColDq, desc_k(sb + C::kOffDs, kk, kPanelBytes),
-                 desc_k(sb + C::kOffK, kk, C::kTPanel), idesc_g, (j > 0 || kk > 0));
+        umma_f16_ts(tmem + C::kColDq, tmem + C::kColDp + ts_col(kk),
+                    desc_mn(k_addr, kk, kPanelBytes), idesc_g, (j > 0 || kk > 0));
       ptx::umma_commit(&bar_mma);
     }
     ok = wait_bar(&bar_mma, ph_mma, p.timeout);
     ph_mma ^= 1;
     ok = __syncthreads_and(ok);
   }
-  if (!ok) {
-    if (r == 0 && p.status) atomicOr(p.status, FA8_DEVERR_TIMEOUT);
-    if (r == 0) {
-      wait_bar(&bar_ld, ph_ld, p.timeout);
-      wait_bar(&bar_ld2, ph_ld2, p.timeout);
-      wait_bar(&bar_mma, ph_mma, p.timeout);
-    }
+  if (!ok && tid == 0) {
+    if (p.status) atomicOr(p.status, FA8_DEVERR_TIMEOUT);
+    wait_bar(&bar_ld[0], 0, p.timeout);
+    wait_bar(&bar_mma, ph_mma, p.timeout);
   }
+  __syncthreads();
   ptx::tc_fence_after();
-  const bool have = ok && n_iter > 0;
-#pragma unroll 1
-  for (int c = 0; c < D / 32; ++c) {
+  if (chunk < D / 32) {
+    const bool have = ok && n_iter > 0;
     uint32_t u[32];
-    ptx::tmem_ld32(tmem + lane_off + C::kColDq + c * 32, u);
+    ptx::tmem_ld32(tmem + lane_off + C::kColDq + chunk * 32, u);
     ptx::tmem_wait_ld();
     ptx::reg_fence32(u);
     if (q < p.sq) {
-      float* dst = p.dq + (row * p.sq + q) * D + c * 32;
+      float* dst = p.dq + (row * p.sq + q) * D + chunk * 32;
 #pragma unroll
       for (int e = 0; e < 32; e += 4)
         *reinterpret_cast<float4*>(dst + e) =
@@ -613,7 +633,7 @@ int map_f16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uin
 }
 
 struct WsLayout {
-  int64_t sqp, skvp, q_el, kv_el, off_q, off_qt, off_k, off_kt, off_v, off_dot, off_delta, total;
+  int64_t sqp, skvp, q_el, kv_el, off_q, off_k, off_v, off_delta, total;
 };
 
 WsLayout ws_layout(const fa8_bwd_params* p) {
@@ -625,11 +645,8 @@ WsLayout ws_layout(const fa8_bwd_params* p) {
   auto al = [](int64_t x) { return (x + 255) / 256 * 256; };
   int64_t o = 0;
   w.off_q = o; o += al(w.q_el * 2);
-  w.off_qt = o; o += al(w.q_el * 2);
   w.off_k = o; o += al(w.kv_el * 2);
-  w.off_kt = o; o += al(w.kv_el * 2);
   w.off_v = o; o += al(w.kv_el * 2);
-  w.off_dot = o; o += al(w.q_el * 2);
   w.off_delta = o; o += al(p->batch * p->heads * w.sqp * 4);
   w.total = o;
   return w;
@@ -654,11 +671,8 @@ int launch(const fa8_bwd_params* p, void* ws, cudaStream_t st) {
   const WsLayout w = ws_layout(p);
   char* base = static_cast<char*>(ws);
   __half* qh = reinterpret_cast<__half*>(base + w.off_q);
-  __half* qt = reinterpret_cast<__half*>(base + w.off_qt);
   __half* kh = reinterpret_cast<__half*>(base + w.off_k);
-  __half* kt = reinterpret_cast<__half*>(base + w.off_kt);
   __half* vh = reinterpret_cast<__half*>(base + w.off_v);
-  __half* dot = reinterpret_cast<__half*>(base + w.off_dot);
   float* delta = reinterpret_cast<float*>(base + w.off_delta);
   const int B = (int)p->batch, H = (int)p->heads, Hk = (int)p->heads_kv;
   const int Sq = (int)p->seqlen_q, Skv = (int)p->seqlen_kv;
@@ -671,29 +685,24 @@ int launch(const fa8_bwd_params* p, void* ws, cudaStream_t st) {
     const uint8_t* q8 = static_cast<const uint8_t*>(p->q);
     const uint8_t* k8 = static_cast<const uint8_t*>(p->k);
     const uint8_t* v8 = static_cast<const uint8_t*>(p->v);
-    bwd_prep_kernel<uint8_t><<<gq, 256, 0, st>>>(q8, q_sb, q_sh, q_ss, 1, H, Sq, Sqp, D, qh, qt);
-    bwd_prep_kernel<uint8_t><<<gk, 256, 0, st>>>(k8, k_sb, k_sh, k_ss, 1, Hk, Skv, Skvp, D, kh, kt);
+    bwd_prep_kernel<uint8_t><<<gq, 256, 0, st>>>(q8, q_sb, q_sh, q_ss, 1, H, Sq, Sqp, D, qh, nullptr);
+    bwd_prep_kernel<uint8_t><<<gk, 256, 0, st>>>(k8, k_sb, k_sh, k_ss, 1, Hk, Skv, Skvp, D, kh, nullptr);
     if (p->v_layout == FA8_V_BHSD)
       bwd_prep_kernel<uint8_t><<<gk, 256, 0, st>>>(v8, k_sb, k_sh, k_ss, 1, Hk, Skv, Skvp, D, vh, nullptr);
     else  // (B, H_kv, D, S_kv): s stride 1, d stride S_kv
       bwd_prep_kernel<uint8_t><<<gk, 256, 0, st>>>(v8, k_sb, k_sh, 1, Skv, Hk, Skv, Skvp, D, vh, nullptr);
-    bwd_prep_kernel<__half><<<gq, 256, 0, st>>>(static_cast<const __half*>(p->d_o), q_sb, q_sh,
-                                                q_ss, 1, H, Sq, Sqp, D, nullptr, dot);
     const long long rows = (long long)B * H * Sqp;
     bwd_delta_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(
         static_cast<const __half*>(p->d_o), static_cast<const __half*>(p->o), delta, H, Sq, Sqp, D, rows);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fa8_note_cuda_error(e, "fa8_bwd prep launch");
   }
-  CUtensorMap tq, tqt, tk, tkt, tv, tdo, tdot;
+  CUtensorMap tq, tk, tv, tdo;
   int rc;
   if ((rc = map_f16(&tq, qh, D, Sqp, H, B, 128)) != FA8_OK) return rc;
   if ((rc = map_f16(&tk, kh, D, Skvp, Hk, B, 128)) != FA8_OK) return rc;
   if ((rc = map_f16(&tv, vh, D, Skvp, Hk, B, 128)) != FA8_OK) return rc;
   if ((rc = map_f16(&tdo, p->d_o, D, Sq, H, B, 128)) != FA8_OK) return rc;
-  if ((rc = map_f16(&tqt, qt, Sqp, D, H, B, D)) != FA8_OK) return rc;
-  if ((rc = map_f16(&tkt, kt, Skvp, D, Hk, B, D)) != FA8_OK) return rc;
-  if ((rc = map_f16(&tdot, dot, Sqp, D, H, B, D)) != FA8_OK) return rc;
 
   Params kp{};
   kp.batch = B; kp.heads = H; kp.heads_kv = Hk; kp.group = H / Hk;
@@ -719,9 +728,9 @@ int launch(const fa8_bwd_params* p, void* ws, cudaStream_t st) {
   });
   if (attr_err[dev] != cudaSuccess) return fa8_note_cuda_error(attr_err[dev], "cudaFuncSetAttribute (bwd)");
   if (Skv > 0 && B > 0)
-    bwd_dkdv_kernel<D><<<dim3(Skvp / 128, Hk, B), 128, DkdvCfg<D>::kSmemAlloc, st>>>(tq, tk, tv, tdo, tqt, tdot, kp);
+    bwd_dkdv_kernel<D><<<dim3(Skvp / 128, Hk, B), kThreadsBwd, DkdvCfg<D>::kSmemAlloc, st>>>(tq, tk, tv, tdo, kp);
   if (Sq > 0 && B > 0)
-    bwd_dq_kernel<D><<<dim3(Sqp / 128, H, B), 128, DqCfg<D>::kSmemAlloc, st>>>(tq, tk, tv, tdo, tkt, kp);
+    bwd_dq_kernel<D><<<dim3(Sqp / 128, H, B), kThreadsBwd, DqCfg<D>::kSmemAlloc, st>>>(tq, tk, tv, tdo, kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fa8_note_cuda_error(e, "fa8_bwd launch");
   fa8_note_launch();

@@ -623,6 +623,26 @@ def aux_kernel_lines(device):
     out["lse_merge"] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
                         "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / hbm,
                         "shape": f"{n} fp32 parts of {rows} rows x 128 -> fp16"}
+    del parts, lses
+    # Backward pass on the headline shape: fp32 dQ/dK/dV from e4m3 Q/K/V, the
+    # forward's fp16 O and LSE and an fp16 dO. Algorithmic work: the five
+    # products of the standard attention backward, 10 * B*H*S^2*D FLOPs (this
+    # implementation also recomputes S and dP in its dQ pass: 14 * B*H*S^2*D
+    # issued).
+    g = torch.Generator(device=device).manual_seed(99)
+    q8 = torch.randn((B, H, S, D), device=device, generator=g).to(torch.float8_e4m3fn)
+    k8 = torch.randn((B, H, S, D), device=device, generator=g).to(torch.float8_e4m3fn)
+    v8 = torch.randn((B, H, D, S), device=device, generator=g).to(torch.float8_e4m3fn)
+    o, lse = fa8.flash_attn_fp8_forward_ex(q8, k8, v8, causal=False, return_lse=True)
+    d_o = torch.randn((B, H, S, D), device=device, generator=g).to(torch.float16)
+    ms = timed(lambda: fa8.flash_attn_fp8_backward(q8, k8, v8, o, d_o, lse, causal=False), reps=5)
+    _, bf16, _ = load_peaks()
+    fl = 10.0 * B * H * S * S * D
+    out["backward"] = {"ms": ms, "tflops": fl / (ms * 1e-3) / 1e12,
+                       "frac_of_bf16_peak": fl / (ms * 1e-3) / 1e12 / bf16,
+                       "flops": fl, "issued_flops": 1.4 * fl,
+                       "shape": f"C2 B{B} H{H} S{S} D{D} non-causal, fp16 tensor-core operands",
+                       "peak_source": "bf16_tflops of MEASURED_PEAKS.json (the f16 product rate)"}
     out["peak_gbs"] = hbm
     out["peak_source"] = f"hbm_gbs of MEASURED_PEAKS.json ({src})"
     return out
