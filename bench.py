@@ -183,7 +183,13 @@ def dist_setup():
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # NCCL's kernels on high-priority streams: the block scheduler then
+        # places the context-parallel K/V transfers ahead of queued attention
+        # CTAs (measured on 2 B200s: point-to-point under a running forward
+        # 156 -> 212 GB/s; 311 GB/s with the GPU otherwise idle).
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), pg_options=opts)
     return world, rank, local
 
 
