@@ -16,17 +16,18 @@
 //      multiple of 128 with zeros. Products that need a tile transposed read
 //      the same copy as an MN-major operand.
 //   2. bwd_delta_kernel: Delta = rowsum(dO * O) in fp32.
-//   3. bwd_dkdv_kernel (one CTA per 128-key tile and KV head): for each query
-//      tile, S^T = K Q^T and dP^T = V dO^T into TMEM (tcgen05, f16 x f16 -> f32);
-//      16 warps (4 per TMEM lane quarter, 32 query columns each) turn them
-//      into fp16 P^T and dS^T written back into TMEM; dV += P^T dO and
-//      dK += dS^T Q then read A from TMEM and accumulate in TMEM.
-//   4. bwd_dq_kernel (one CTA per 128-query tile and head): for each key tile,
-//      S = Q K^T and dP = dO V^T, dS in fp16 (TMEM), dQ += dS K in TMEM.
-// Operands move by TMA into 128B-swizzled 64-column panels, the next
-// iteration's tiles into a second buffer while this one computes; one thread
-// issues the tcgen05 products; every wait is bounded and reports a timeout in
-// the status word instead of hanging.
+//   3. bwd_tile_kernel<D, false> (dK, dV; one CTA per 128-key tile and KV
+//      head): for each query tile, S^T = K Q^T and dP^T = V dO^T into TMEM
+//      (tcgen05, f16 x f16 -> f32), turned into fp16 P^T and dS^T in TMEM by
+//      16 warps; dV += P^T dO and dK += dS^T Q read A from TMEM and
+//      accumulate in TMEM.
+//   4. bwd_tile_kernel<D, true> (dQ; one CTA per 128-query tile and head):
+//      for each key tile, S = Q K^T, dP = dO V^T, dS in fp16, dQ += dS K.
+// Warp-specialised: a TMA warp streams the tiles (double-buffered), one thread
+// issues every product, and the streamed tile is split into two 64-column
+// halves so that one half's elementwise pass overlaps the other half's
+// products. Every wait is bounded and reports a timeout in the status word
+// instead of hanging.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -179,9 +180,6 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(const __half* d_o, const
 }
 
 // ------------------------------------------------------------------ shared parts
-constexpr int kThreadsBwd = 512;  // 16 warps: warp w reads TMEM lanes 32 (w % 4) .. +31
-                                  // and key / query columns 32 (w / 4) .. +31
-
 // Warp-collective store of 16 consecutive 32-bit TMEM columns (one per register).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -207,53 +205,99 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 // pass wrote as 16-column blocks at the start of each 32-column chunk.
 __device__ __forceinline__ uint32_t ts_col(int kk) { return 32u * (kk >> 1) + 8u * (kk & 1); }
 
-// ------------------------------------------------------------------ dK, dV
-template <int D>
-struct DkdvCfg {
-  static constexpr int kRowTile = kTile * D * 2;     // [128][D] fp16 (D / 64 panels)
-  static constexpr int kOffK = 0;
-  static constexpr int kOffV = kOffK + kRowTile;
-  static constexpr int kOffQ = kOffV + kRowTile;     // two buffers: Q_i, Q_i+1
-  static constexpr int kOffDo = kOffQ + 2 * kRowTile;  // two buffers: dO_i, dO_i+1
-  static constexpr int kOffLse = kOffDo + 2 * kRowTile;  // 128 floats: LSE * log2(e)
-  static constexpr int kOffDelta = kOffLse + 512;
-  static constexpr int kSmem = kOffDelta + 512;
+// ------------------------------------------------------------------ tile kernel
+// One kernel body for both passes. A CTA owns a fixed 128-row tile (dK/dV:
+// 128 keys of one K/V head; dQ: 128 queries of one head) and streams 128-column
+// tiles of the other side (query tiles of every head of the group; key tiles).
+// Each streamed tile is handled as two 64-column halves that ping-pong: while
+// 8 warps turn half a's S/dP into fp16 P/dS, the tensor pipe runs half b's
+// products, and the reverse.
+//   warps 0-15  elementwise: half h = w / 8, TMEM lanes 32 (w % 4) .., columns
+//               32 ((w / 4) % 2) .. of the half
+//   warp 16     TMA producer (lane 0)
+//   warp 17     TMEM allocation; lane 0 issues every tcgen05.mma
+// TMEM columns: half h: S at 128 h, dP at 128 h + 64 (P, dS written back into
+// the first 16 columns of each 32-column chunk); accumulators at 256 (dV or
+// dQ) and 256 + D (dK).
+constexpr int kWarpsEw = 16;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kThreadsTile = 18 * 32;
+
+template <int D, bool kDq>
+struct TileCfg {
+  static constexpr int kRowTile = kTile * D * 2;          // [128][D] fp16 (D / 64 panels)
+  static constexpr int kOffA = 0;                         // fixed: K (dkdv) or Q (dq)
+  static constexpr int kOffA2 = kOffA + kRowTile;         // fixed: V (dkdv) or dO (dq)
+  static constexpr int kOffB = kOffA2 + kRowTile;         // streamed: Q / K, two buffers
+  static constexpr int kOffB2 = kOffB + 2 * kRowTile;     // streamed: dO / V, two buffers
+  static constexpr int kSmem = kOffB2 + 2 * kRowTile;
   static constexpr int kSmemAlloc = kSmem + 1024;
-  // TMEM: S^T (then P^T) | dP^T (then dS^T) | dV | dK
-  static constexpr uint32_t kColS = 0, kColDp = 128, kColDv = 256, kColDk = 256 + D;
+  static constexpr uint32_t kColAcc1 = 256, kColAcc2 = 256 + D;
 };
 
-template <int D>
-__global__ void __launch_bounds__(kThreadsBwd, 1)
-    bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+struct TileBars {
+  uint64_t fixed_full;
+  uint64_t ld_full[2], ld_empty[2];
+  uint64_t s_full[2], p_full[2], e_done[2];
+  uint64_t acc_done;
+};
+
+__device__ __forceinline__ bool wait_bar_abort(uint64_t* bar, uint32_t parity, long long limit,
+                                               volatile int* abort_flag) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > limit) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+template <int D, bool kDq>
+__global__ void __launch_bounds__(kThreadsTile, 1)
+    bwd_tile_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                     const Params p) {
-  using C = DkdvCfg<D>;
+  using C = TileCfg<D, kDq>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_ld[2], bar_mma;
+  __shared__ TileBars bars;
   __shared__ uint32_t tmem_sh;
+  __shared__ int abort_sh;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sb = ptx::smem_u32(smem);
-  float* lse_sh = reinterpret_cast<float*>(smem + C::kOffLse);
-  float* delta_sh = reinterpret_cast<float*>(smem + C::kOffDelta);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int quad = warp & 3, chunk = warp >> 2;
-  const int r = quad * 32 + lane;  // key row of the tile == TMEM lane
-  const int j = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
-  const int key = j * kTile + r;
-  const int nq = (p.sq + kTile - 1) / kTile;
-  const int i_lo = p.causal ? j : 0;
-  const int n_heads = p.group;
-  const int n_iter = (i_lo < nq ? nq - i_lo : 0) * n_heads;
+  // Fixed tile: blockIdx.x = tile, y = head (K/V head for dK/dV), z = batch.
+  const int fx = blockIdx.x, hy = blockIdx.y, b = blockIdx.z;
+  int n_iter, i_lo = 0;
+  if constexpr (kDq) {
+    const int nkv = (p.skv + kTile - 1) / kTile;
+    n_iter = p.causal ? min(fx + 1, nkv) : nkv;
+  } else {
+    const int nq = (p.sq + kTile - 1) / kTile;
+    i_lo = p.causal ? fx : 0;
+    n_iter = (i_lo < nq ? nq - i_lo : 0) * p.group;
+  }
+  volatile int* abort_flag = &abort_sh;
 
   if (tid == 0) {
-    ptx::mbar_init(&bar_ld[0], 1);
-    ptx::mbar_init(&bar_ld[1], 1);
-    ptx::mbar_init(&bar_mma, 1);
+    ptx::mbar_init(&bars.fixed_full, 1);
+    for (int x = 0; x < 2; ++x) {
+      ptx::mbar_init(&bars.ld_full[x], 1);
+      ptx::mbar_init(&bars.ld_empty[x], 1);
+      ptx::mbar_init(&bars.s_full[x], 1);
+      ptx::mbar_init(&bars.p_full[x], 8);
+      ptx::mbar_init(&bars.e_done[x], 1);
+    }
+    ptx::mbar_init(&bars.acc_done, 1);
+    abort_sh = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     ptx::tmem_alloc(&tmem_sh, 512);
     ptx::tmem_relinquish();
   }
@@ -261,333 +305,263 @@ __global__ void __launch_bounds__(kThreadsBwd, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = tmem_sh;
-  const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-  constexpr uint32_t idesc_s = idesc_f16_f32(128, 128);
-  constexpr uint32_t idesc_g = ptx::idesc_e4m3_f32(128, D, true);  // B MN-major
-  uint32_t ph_mma = 0;
   bool ok = true;
 
-  // Q_i and dO_i of iteration `it` into buffer it & 1 (K_j, V_j with the first).
-  auto issue_loads = [&](int it) {
-    const int i = i_lo + it / n_heads;
-    const int h = hk * p.group + it % n_heads;
-    const int buf = it & 1;
-    uint32_t bytes = 2 * C::kRowTile;
-    if (it == 0) bytes += 2 * C::kRowTile;
-    ptx::mbar_arrive_expect_tx(&bar_ld[buf], bytes);
-    const uint64_t pol = ptx::policy_evict_last();
-#pragma unroll
-    for (int pnl = 0; pnl < D / 64; ++pnl) {
-      if (it == 0) {
-        ptx::tma_load_4d(smem + C::kOffK + pnl * kPanelBytes, &tm_k, &bar_ld[buf], pnl * 64, j * kTile, hk, b, pol);
-        ptx::tma_load_4d(smem + C::kOffV + pnl * kPanelBytes, &tm_v, &bar_ld[buf], pnl * 64, j * kTile, hk, b, pol);
-      }
-      ptx::tma_load_4d(smem + C::kOffQ + buf * C::kRowTile + pnl * kPanelBytes, &tm_q, &bar_ld[buf],
-                       pnl * 64, i * kTile, h, b, pol);
-      ptx::tma_load_4d(smem + C::kOffDo + buf * C::kRowTile + pnl * kPanelBytes, &tm_do, &bar_ld[buf],
-                       pnl * 64, i * kTile, h, b, pol);
+  // Streamed tile t: (query tile, head) for dK/dV, key tile for dQ.
+  auto stream_coords = [&](int t, int& row_tile, int& head) {
+    if constexpr (kDq) {
+      row_tile = t;
+      head = hy / p.group;
+    } else {
+      row_tile = i_lo + t / p.group;
+      head = hy * p.group + t % p.group;
     }
   };
-  if (tid == 0 && n_iter > 0) issue_loads(0);
 
-  for (int it = 0; it < n_iter && ok; ++it) {
-    const int i = i_lo + it / n_heads;
-    const int h = hk * p.group + it % n_heads;
-    const int buf = it & 1;
-    // The other buffer was last read by the products of iteration it - 1 (complete).
-    if (tid == 0 && it + 1 < n_iter) issue_loads(it + 1);
-    if (tid < kTile) {
-      const int q = i * kTile + tid;
-      const long long row = ((long long)b * p.heads + h);
-      const float l = q < p.sq ? p.lse[row * p.sq + q] : INFINITY;
-      lse_sh[tid] = (l == -INFINITY) ? INFINITY : l * 1.4426950408889634f;
-      delta_sh[tid] = p.delta[row * p.sqp + i * kTile + tid];
-    }
-    ok = wait_bar(&bar_ld[buf], (uint32_t)(it >> 1) & 1u, p.timeout);
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    const uint32_t q_addr = sb + C::kOffQ + buf * C::kRowTile;
-    const uint32_t do_addr = sb + C::kOffDo + buf * C::kRowTile;
-    // S^T = K Q^T, dP^T = V dO^T
-    if (tid == 0) {
-      ptx::tc_fence_after();
+  if (warp == kProducerWarp) {
+    if (lane == 0 && n_iter > 0) {
+      const uint64_t pol = ptx::policy_evict_last();
+      ptx::mbar_arrive_expect_tx(&bars.fixed_full, 2 * C::kRowTile);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        umma_f16(tmem + C::kColS, desc_k(sb + C::kOffK, kk, kPanelBytes),
-                 desc_k(q_addr, kk, kPanelBytes), idesc_s, kk > 0);
-        umma_f16(tmem + C::kColDp, desc_k(sb + C::kOffV, kk, kPanelBytes),
-                 desc_k(do_addr, kk, kPanelBytes), idesc_s, kk > 0);
+      for (int pnl = 0; pnl < D / 64; ++pnl) {
+        if constexpr (kDq) {
+          ptx::tma_load_4d(smem + C::kOffA + pnl * kPanelBytes, &tm_q, &bars.fixed_full, pnl * 64, fx * kTile, hy, b, pol);
+          ptx::tma_load_4d(smem + C::kOffA2 + pnl * kPanelBytes, &tm_do, &bars.fixed_full, pnl * 64, fx * kTile, hy, b, pol);
+        } else {
+          ptx::tma_load_4d(smem + C::kOffA + pnl * kPanelBytes, &tm_k, &bars.fixed_full, pnl * 64, fx * kTile, hy, b, pol);
+          ptx::tma_load_4d(smem + C::kOffA2 + pnl * kPanelBytes, &tm_v, &bars.fixed_full, pnl * 64, fx * kTile, hy, b, pol);
+        }
       }
-      ptx::umma_commit(&bar_mma);
+      int issued = 0;
+      for (int t = 0; t < n_iter; ++t) {
+        const int buf = t & 1;
+        if (t >= 2 &&
+            !wait_bar_abort(&bars.ld_empty[buf], (uint32_t)((t >> 1) - 1) & 1u, p.timeout, abort_flag))
+          break;
+        int rt, hh;
+        stream_coords(t, rt, hh);
+        ptx::mbar_arrive_expect_tx(&bars.ld_full[buf], 2 * C::kRowTile);
+#pragma unroll
+        for (int pnl = 0; pnl < D / 64; ++pnl) {
+          uint8_t* d1 = smem + C::kOffB + buf * C::kRowTile + pnl * kPanelBytes;
+          uint8_t* d2 = smem + C::kOffB2 + buf * C::kRowTile + pnl * kPanelBytes;
+          if constexpr (kDq) {
+            ptx::tma_load_4d(d1, &tm_k, &bars.ld_full[buf], pnl * 64, rt * kTile, hh, b, pol);
+            ptx::tma_load_4d(d2, &tm_v, &bars.ld_full[buf], pnl * 64, rt * kTile, hh, b, pol);
+          } else {
+            ptx::tma_load_4d(d1, &tm_q, &bars.ld_full[buf], pnl * 64, rt * kTile, hh, b, pol);
+            ptx::tma_load_4d(d2, &tm_do, &bars.ld_full[buf], pnl * 64, rt * kTile, hh, b, pol);
+          }
+        }
+        ++issued;
+      }
+      // Copies still in flight must land before the CTA exits (bounded waits).
+      for (int t = max(0, issued - 2); t < issued; ++t) {
+        const long long t0 = clock64();
+        while (!ptx::mbar_try_wait(&bars.ld_full[t & 1], (uint32_t)(t >> 1) & 1u) &&
+               clock64() - t0 < p.timeout) {
+        }
+      }
+      {
+        const long long t0 = clock64();
+        while (!ptx::mbar_try_wait(&bars.fixed_full, 0) && clock64() - t0 < p.timeout) {
+        }
+      }
     }
-    ok = wait_bar(&bar_mma, ph_mma, p.timeout);
-    ph_mma ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    // P^T and dS^T of this warp's 32 queries, fp16, back into the first 16
-    // columns of the chunk they were read from.
-    ptx::tc_fence_after();
-    {
+  } else if (warp == kMmaWarp) {
+    if (lane == 0 && n_iter > 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, 64);
+      constexpr uint32_t idesc_e = ptx::idesc_e4m3_f32(128, D, true);  // B MN-major
+      const uint32_t a1 = sb + C::kOffA, a2 = sb + C::kOffA2;
+      ok = wait_bar_abort(&bars.fixed_full, 0, p.timeout, abort_flag);
+      // S_h(t) = A1 B1_h^T, dP_h(t) = A2 B2_h^T (64 columns each)
+      auto issue_s = [&](int t, int h) -> bool {
+        const int buf = t & 1;
+        if (h == 0 && !wait_bar_abort(&bars.ld_full[buf], (uint32_t)(t >> 1) & 1u, p.timeout, abort_flag))
+          return false;
+        ptx::tc_fence_after();
+        const uint32_t b1 = sb + C::kOffB + buf * C::kRowTile + h * 8192;
+        const uint32_t b2 = sb + C::kOffB2 + buf * C::kRowTile + h * 8192;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16(tmem + 128 * h, desc_k(a1, kk, kPanelBytes), desc_k(b1, kk, kPanelBytes), idesc_s, kk > 0);
+          umma_f16(tmem + 128 * h + 64, desc_k(a2, kk, kPanelBytes), desc_k(b2, kk, kPanelBytes), idesc_s, kk > 0);
+        }
+        ptx::umma_commit(&bars.s_full[h]);
+        return true;
+      };
+      // Accumulator products of half h of tile t (K = 64 columns of the half).
+      auto issue_e = [&](int t, int h) -> bool {
+        if (!wait_bar_abort(&bars.p_full[h], (uint32_t)t & 1u, p.timeout, abort_flag)) return false;
+        ptx::tc_fence_after();
+        const int buf = t & 1;
+        const uint32_t b1 = sb + C::kOffB + buf * C::kRowTile;   // Q_t or K_t
+        const uint32_t b2 = sb + C::kOffB2 + buf * C::kRowTile;  // dO_t
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acc = (t > 0 || h > 0 || kk > 0) ? 1u : 0u;
+          if constexpr (kDq) {
+            umma_f16_ts(tmem + C::kColAcc1, tmem + 128 * h + 64 + ts_col(kk),
+                        desc_mn(b1, kk + 4 * h, kPanelBytes), idesc_e, acc);
+          } else {
+            umma_f16_ts(tmem + C::kColAcc1, tmem + 128 * h + ts_col(kk),
+                        desc_mn(b2, kk + 4 * h, kPanelBytes), idesc_e, acc);
+            umma_f16_ts(tmem + C::kColAcc2, tmem + 128 * h + 64 + ts_col(kk),
+                        desc_mn(b1, kk + 4 * h, kPanelBytes), idesc_e, acc);
+          }
+        }
+        ptx::umma_commit(&bars.e_done[h]);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0) && issue_s(0, 1);
+      for (int t = 0; t < n_iter && ok; ++t) {
+        ok = issue_e(t, 0);
+        if (!ok) break;
+        if (t + 1 < n_iter) {
+          ok = wait_bar_abort(&bars.e_done[0], (uint32_t)t & 1u, p.timeout, abort_flag) && issue_s(t + 1, 0);
+          if (!ok) break;
+        }
+        ok = issue_e(t, 1);
+        if (!ok) break;
+        ptx::umma_commit(&bars.ld_empty[t & 1]);
+        if (t + 1 < n_iter) {
+          ok = wait_bar_abort(&bars.e_done[1], (uint32_t)t & 1u, p.timeout, abort_flag) && issue_s(t + 1, 1);
+          if (!ok) break;
+        }
+      }
+      ptx::umma_commit(&bars.acc_done);
+      // Drain: every product issued here completes before TMEM is freed.
+      const long long t0 = clock64();
+      while (!ptx::mbar_try_wait(&bars.acc_done, 0) && clock64() - t0 < p.timeout) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------ elementwise warps
+    const int h = warp >> 3, quad = warp & 3, chunk = (warp >> 2) & 1;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t col_s = 128 * h + 32 * chunk, col_dp = col_s + 64;
+    const int row_g = fx * kTile + r;  // key (dK/dV) or query (dQ) of this TMEM lane
+    float row_lse2 = INFINITY, row_delta = 0.f;
+    if constexpr (kDq) {
+      if (row_g < p.sq) {
+        const long long rr = (long long)b * p.heads + hy;
+        const float l = p.lse[rr * p.sq + row_g];
+        row_lse2 = (l == -INFINITY) ? INFINITY : l * 1.4426950408889634f;
+        row_delta = p.delta[rr * p.sqp + row_g];
+      }
+    }
+    for (int t = 0; t < n_iter && ok; ++t) {
+      int rt, hh;
+      stream_coords(t, rt, hh);
+      const int c0 = rt * kTile + 64 * h + 32 * chunk;  // first column (query / key) of this warp
+      float lse2_l = INFINITY, delta_l = 0.f;             // dK/dV: this lane's column
+      if constexpr (!kDq) {
+        const int qc = c0 + lane;
+        const long long rr = (long long)b * p.heads + hh;
+        if (qc < p.sq) {
+          const float l = __ldg(p.lse + rr * p.sq + qc);
+          lse2_l = (l == -INFINITY) ? INFINITY : l * 1.4426950408889634f;
+        }
+        delta_l = __ldg(p.delta + rr * p.sqp + qc);
+      }
+      ok = wait_bar_abort(&bars.s_full[h], (uint32_t)t & 1u, p.timeout, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      ptx::tc_fence_after();
       uint32_t us[32], ud[32];
-      ptx::tmem_ld32(tmem + lane_off + C::kColS + chunk * 32, us);
-      ptx::tmem_ld32(tmem + lane_off + C::kColDp + chunk * 32, ud);
+      ptx::tmem_ld32(tmem + lane_off + col_s, us);
+      ptx::tmem_ld32(tmem + lane_off + col_dp, ud);
       ptx::tmem_wait_ld();
       ptx::reg_fence32(us);
       ptx::reg_fence32(ud);
-      const int q0 = i * kTile + chunk * 32;
-      const bool full = key < p.skv && q0 + 31 < p.sq && (!p.causal || key <= q0);
+      bool full;
+      if constexpr (kDq)
+        full = row_g < p.sq && c0 + 31 < p.skv && (!p.causal || c0 + 31 <= row_g);
+      else
+        full = row_g < p.skv && c0 + 31 < p.sq && (!p.causal || row_g <= c0);
       uint32_t hp[16], hd[16];
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
         float pv[2], dv[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const int qc = chunk * 32 + e + u;
-          const int q = q0 + e + u;
-          const bool valid = full || (key < p.skv && q < p.sq && (!p.causal || key <= q));
-          const float pr = valid ? ptx::ex2(__uint_as_float(us[e + u]) * p.sl2 - lse_sh[qc]) : 0.f;
+          const int col = c0 + e + u;
+          float l2, dl;
+          bool valid;
+          if constexpr (kDq) {
+            l2 = row_lse2;
+            dl = row_delta;
+            valid = full || (col < p.skv && row_g < p.sq && (!p.causal || col <= row_g));
+          } else {
+            l2 = __shfl_sync(0xffffffffu, lse2_l, e + u);
+            dl = __shfl_sync(0xffffffffu, delta_l, e + u);
+            valid = full || (row_g < p.skv && col < p.sq && (!p.causal || row_g <= col));
+          }
+          const float pr = valid ? ptx::ex2(__uint_as_float(us[e + u]) * p.sl2 - l2) : 0.f;
           pv[u] = pr;
-          dv[u] = pr * (__uint_as_float(ud[e + u]) - delta_sh[qc]);
+          dv[u] = pr * (__uint_as_float(ud[e + u]) - dl);
         }
         hp[e / 2] = pack_h2(pv[0], pv[1]);
         hd[e / 2] = pack_h2(dv[0], dv[1]);
       }
-      tmem_st16(tmem + lane_off + C::kColS + chunk * 32, hp);
-      tmem_st16(tmem + lane_off + C::kColDp + chunk * 32, hd);
+      if constexpr (!kDq) tmem_st16(tmem + lane_off + col_s, hp);
+      tmem_st16(tmem + lane_off + col_dp, hd);
       ptx::tmem_wait_st();
-    }
-    ptx::tc_fence_before();
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    // dV += P^T dO, dK += dS^T Q (K = the 128 queries of the tile)
-    if (tid == 0) {
-      ptx::tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < kTile / 16; ++kk) {
-        umma_f16_ts(tmem + C::kColDv, tmem + C::kColS + ts_col(kk),
-                    desc_mn(do_addr, kk, kPanelBytes), idesc_g, (it > 0 || kk > 0));
-        umma_f16_ts(tmem + C::kColDk, tmem + C::kColDp + ts_col(kk),
-                    desc_mn(q_addr, kk, kPanelBytes), idesc_g, (it > 0 || kk > 0));
-      }
-      ptx::umma_commit(&bar_mma);
-    }
-    ok = wait_bar(&bar_mma, ph_mma, p.timeout);
-    ph_mma ^= 1;
-    ok = __syncthreads_and(ok);
-  }
-  if (!ok && tid == 0) {
-    if (p.status) atomicOr(p.status, FA8_DEVERR_TIMEOUT);
-    // Let copies and products in flight finish (bounded) before TMEM is freed.
-    wait_bar(&bar_ld[0], 0, p.timeout);
-    wait_bar(&bar_mma, ph_mma, p.timeout);
-  }
-  __syncthreads();
-  // Epilogue: dV and scale * dK rows of this key tile (zero when no query sees them).
-  ptx::tc_fence_after();
-  if (chunk < D / 32) {
-    const bool have = ok && n_iter > 0;
-    const long long row_off = (((long long)b * p.heads_kv + hk) * p.skv + key) * D + chunk * 32;
-    uint32_t uv[32], uk[32];
-    ptx::tmem_ld32(tmem + lane_off + C::kColDv + chunk * 32, uv);
-    ptx::tmem_ld32(tmem + lane_off + C::kColDk + chunk * 32, uk);
-    ptx::tmem_wait_ld();
-    ptx::reg_fence32(uv);
-    ptx::reg_fence32(uk);
-    if (key < p.skv) {
-#pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        const float4 a = have ? make_float4(__uint_as_float(uv[e]), __uint_as_float(uv[e + 1]),
-                                            __uint_as_float(uv[e + 2]), __uint_as_float(uv[e + 3]))
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 k4 =
-            have ? make_float4(__uint_as_float(uk[e]) * p.scale, __uint_as_float(uk[e + 1]) * p.scale,
-                               __uint_as_float(uk[e + 2]) * p.scale, __uint_as_float(uk[e + 3]) * p.scale)
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(p.dv + row_off + e) = a;
-        *reinterpret_cast<float4*>(p.dk + row_off + e) = k4;
-      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars.p_full[h]);
     }
   }
-  ptx::tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
+
+  // Epilogue: the accumulators, 32 columns per warp (warps 0..D/32-1 of each lane quarter).
+  if (warp < kWarpsEw) {
+    const int quad = warp & 3, c4 = warp >> 2;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int row_g = fx * kTile + quad * 32 + lane;
+    if (n_iter > 0) ok = ok && wait_bar_abort(&bars.acc_done, 0, p.timeout, abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, 512);
-  }
-}
-
-// ------------------------------------------------------------------ dQ
-template <int D>
-struct DqCfg {
-  static constexpr int kRowTile = kTile * D * 2;
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffDo = kOffQ + kRowTile;
-  static constexpr int kOffK = kOffDo + kRowTile;    // two buffers: K_j, K_j+1
-  static constexpr int kOffV = kOffK + 2 * kRowTile;  // two buffers: V_j, V_j+1
-  static constexpr int kSmem = kOffV + 2 * kRowTile;
-  static constexpr int kSmemAlloc = kSmem + 1024;
-  // TMEM: S | dP (then dS) | dQ
-  static constexpr uint32_t kColS = 0, kColDp = 128, kColDq = 256;
-};
-
-template <int D>
-__global__ void __launch_bounds__(kThreadsBwd, 1)
-    bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                  const Params p) {
-  using C = DqCfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_ld[2], bar_mma;
-  __shared__ uint32_t tmem_sh;
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  const uint32_t sb = ptx::smem_u32(smem);
-  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int quad = warp & 3, chunk = warp >> 2;
-  const int r = quad * 32 + lane;  // query row of the tile == TMEM lane
-  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int hk = h / p.group;
-  const int q = i * kTile + r;
-  const int nkv = (p.skv + kTile - 1) / kTile;
-  const int n_iter = p.causal ? min(i + 1, nkv) : nkv;
-  const long long row = (long long)b * p.heads + h;
-  float lse2 = INFINITY, delta = 0.f;
-  if (q < p.sq) {
-    const float l = p.lse[row * p.sq + q];
-    lse2 = (l == -INFINITY) ? INFINITY : l * 1.4426950408889634f;
-    delta = p.delta[row * p.sqp + q];
-  }
-
-  if (tid == 0) {
-    ptx::mbar_init(&bar_ld[0], 1);
-    ptx::mbar_init(&bar_ld[1], 1);
-    ptx::mbar_init(&bar_mma, 1);
-    ptx::fence_mbar_init();
-  }
-  if (warp == 0) {
-    ptx::tmem_alloc(&tmem_sh, 512);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem = tmem_sh;
-  const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-  constexpr uint32_t idesc_s = idesc_f16_f32(128, 128);
-  constexpr uint32_t idesc_g = ptx::idesc_e4m3_f32(128, D, true);  // B MN-major
-  uint32_t ph_mma = 0;
-  bool ok = true;
-
-  auto issue_loads = [&](int jj) {
-    const int buf = jj & 1;
-    uint32_t bytes = 2 * C::kRowTile;
-    if (jj == 0) bytes += 2 * C::kRowTile;
-    ptx::mbar_arrive_expect_tx(&bar_ld[buf], bytes);
-    const uint64_t pol = ptx::policy_evict_last();
-#pragma unroll
-    for (int pnl = 0; pnl < D / 64; ++pnl) {
-      if (jj == 0) {
-        ptx::tma_load_4d(smem + C::kOffQ + pnl * kPanelBytes, &tm_q, &bar_ld[buf], pnl * 64, i * kTile, h, b, pol);
-        ptx::tma_load_4d(smem + C::kOffDo + pnl * kPanelBytes, &tm_do, &bar_ld[buf], pnl * 64, i * kTile, h, b, pol);
-      }
-      ptx::tma_load_4d(smem + C::kOffK + buf * C::kRowTile + pnl * kPanelBytes, &tm_k, &bar_ld[buf],
-                       pnl * 64, jj * kTile, hk, b, pol);
-      ptx::tma_load_4d(smem + C::kOffV + buf * C::kRowTile + pnl * kPanelBytes, &tm_v, &bar_ld[buf],
-                       pnl * 64, jj * kTile, hk, b, pol);
-    }
-  };
-  if (tid == 0 && n_iter > 0) issue_loads(0);
-
-  for (int j = 0; j < n_iter && ok; ++j) {
-    const int buf = j & 1;
-    if (tid == 0 && j + 1 < n_iter) issue_loads(j + 1);
-    ok = wait_bar(&bar_ld[buf], (uint32_t)(j >> 1) & 1u, p.timeout);
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    const uint32_t k_addr = sb + C::kOffK + buf * C::kRowTile;
-    const uint32_t v_addr = sb + C::kOffV + buf * C::kRowTile;
-    if (tid == 0) {
-      ptx::tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        umma_f16(tmem + C::kColS, desc_k(sb + C::kOffQ, kk, kPanelBytes),
-                 desc_k(k_addr, kk, kPanelBytes), idesc_s, kk > 0);
-        umma_f16(tmem + C::kColDp, desc_k(sb + C::kOffDo, kk, kPanelBytes),
-                 desc_k(v_addr, kk, kPanelBytes), idesc_s, kk > 0);
-      }
-      ptx::umma_commit(&bar_mma);
-    }
-    ok = wait_bar(&bar_mma, ph_mma, p.timeout);
-    ph_mma ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    ptx::tc_fence_after();
-    {
-      uint32_t us[32], ud[32];
-      ptx::tmem_ld32(tmem + lane_off + C::kColS + chunk * 32, us);
-      ptx::tmem_ld32(tmem + lane_off + C::kColDp + chunk * 32, ud);
+    if (c4 < D / 32) {
+      const bool have = ok && n_iter > 0 && !*abort_flag;
+      uint32_t u1[32], u2[32];
+      ptx::tmem_ld32(tmem + lane_off + C::kColAcc1 + c4 * 32, u1);
+      if constexpr (!kDq) ptx::tmem_ld32(tmem + lane_off + C::kColAcc2 + c4 * 32, u2);
       ptx::tmem_wait_ld();
-      ptx::reg_fence32(us);
-      ptx::reg_fence32(ud);
-      const int k0 = j * kTile + chunk * 32;
-      const bool full = q < p.sq && k0 + 31 < p.skv && (!p.causal || k0 + 31 <= q);
-      uint32_t hd[16];
+      ptx::reg_fence32(u1);
+      if constexpr (!kDq) ptx::reg_fence32(u2);
+      if constexpr (kDq) {
+        if (row_g < p.sq) {
+          float* dst = p.dq + (((long long)b * p.heads + hy) * p.sq + row_g) * D + c4 * 32;
 #pragma unroll
-      for (int e = 0; e < 32; e += 2) {
-        float dv[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int key = k0 + e + u;
-          const bool valid = full || (key < p.skv && q < p.sq && (!p.causal || key <= q));
-          const float pr = valid ? ptx::ex2(__uint_as_float(us[e + u]) * p.sl2 - lse2) : 0.f;
-          dv[u] = pr * (__uint_as_float(ud[e + u]) - delta);
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(dst + e) =
+                have ? make_float4(__uint_as_float(u1[e]) * p.scale, __uint_as_float(u1[e + 1]) * p.scale,
+                                   __uint_as_float(u1[e + 2]) * p.scale, __uint_as_float(u1[e + 3]) * p.scale)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        hd[e / 2] = pack_h2(dv[0], dv[1]);
+      } else {
+        if (row_g < p.skv) {
+          const long long off = (((long long)b * p.heads_kv + hy) * p.skv + row_g) * D + c4 * 32;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            *reinterpret_cast<float4*>(p.dv + off + e) =
+                have ? make_float4(__uint_as_float(u1[e]), __uint_as_float(u1[e + 1]),
+                                   __uint_as_float(u1[e + 2]), __uint_as_float(u1[e + 3]))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(p.dk + off + e) =
+                have ? make_float4(__uint_as_float(u2[e]) * p.scale, __uint_as_float(u2[e + 1]) * p.scale,
+                                   __uint_as_float(u2[e + 2]) * p.scale, __uint_as_float(u2[e + 3]) * p.scale)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
       }
-      tmem_st16(tmem + lane_off + C::kColDp + chunk * 32, hd);
-      ptx::tmem_wait_st();
-    }
-    ptx::tc_fence_before();
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    if (tid == 0) {
-      ptx::tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < kTile / 16; ++kk)
-        umma_f16_ts(tmem + C::kColDq, tmem + C::kColDp + ts_col(kk),
-                    desc_mn(k_addr, kk, kPanelBytes), idesc_g, (j > 0 || kk > 0));
-      ptx::umma_commit(&bar_mma);
-    }
-    ok = wait_bar(&bar_mma, ph_mma, p.timeout);
-    ph_mma ^= 1;
-    ok = __syncthreads_and(ok);
-  }
-  if (!ok && tid == 0) {
-    if (p.status) atomicOr(p.status, FA8_DEVERR_TIMEOUT);
-    wait_bar(&bar_ld[0], 0, p.timeout);
-    wait_bar(&bar_mma, ph_mma, p.timeout);
-  }
-  __syncthreads();
-  ptx::tc_fence_after();
-  if (chunk < D / 32) {
-    const bool have = ok && n_iter > 0;
-    uint32_t u[32];
-    ptx::tmem_ld32(tmem + lane_off + C::kColDq + chunk * 32, u);
-    ptx::tmem_wait_ld();
-    ptx::reg_fence32(u);
-    if (q < p.sq) {
-      float* dst = p.dq + (row * p.sq + q) * D + chunk * 32;
-#pragma unroll
-      for (int e = 0; e < 32; e += 4)
-        *reinterpret_cast<float4*>(dst + e) =
-            have ? make_float4(__uint_as_float(u[e]) * p.scale, __uint_as_float(u[e + 1]) * p.scale,
-                               __uint_as_float(u[e + 2]) * p.scale, __uint_as_float(u[e + 3]) * p.scale)
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
+  if (tid == 0 && *abort_flag && p.status) atomicOr(p.status, FA8_DEVERR_TIMEOUT);
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, 512);
   }
@@ -720,17 +694,21 @@ int launch(const fa8_bwd_params* p, void* ws, cudaStream_t st) {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return fa8_note_error(FA8_ERR_INVALID_ARG, "device index out of range");
   std::call_once(once[dev], [dev] {
-    cudaError_t e1 = cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          DkdvCfg<D>::kSmemAlloc);
-    cudaError_t e2 = cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          DqCfg<D>::kSmemAlloc);
+    cudaError_t e1 = cudaFuncSetAttribute(bwd_tile_kernel<D, false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          TileCfg<D, false>::kSmemAlloc);
+    cudaError_t e2 = cudaFuncSetAttribute(bwd_tile_kernel<D, true>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          TileCfg<D, true>::kSmemAlloc);
     attr_err[dev] = e1 != cudaSuccess ? e1 : e2;
   });
   if (attr_err[dev] != cudaSuccess) return fa8_note_cuda_error(attr_err[dev], "cudaFuncSetAttribute (bwd)");
   if (Skv > 0 && B > 0)
-    bwd_dkdv_kernel<D><<<dim3(Skvp / 128, Hk, B), kThreadsBwd, DkdvCfg<D>::kSmemAlloc, st>>>(tq, tk, tv, tdo, kp);
+    bwd_tile_kernel<D, false><<<dim3(Skvp / 128, Hk, B), kThreadsTile, TileCfg<D, false>::kSmemAlloc, st>>>(
+        tq, tk, tv, tdo, kp);
   if (Sq > 0 && B > 0)
-    bwd_dq_kernel<D><<<dim3(Sqp / 128, H, B), kThreadsBwd, DqCfg<D>::kSmemAlloc, st>>>(tq, tk, tv, tdo, kp);
+    bwd_tile_kernel<D, true><<<dim3(Sqp / 128, H, B), kThreadsTile, TileCfg<D, true>::kSmemAlloc, st>>>(
+        tq, tk, tv, tdo, kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fa8_note_cuda_error(e, "fa8_bwd launch");
   fa8_note_launch();
