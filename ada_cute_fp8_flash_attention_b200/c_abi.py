@@ -32,6 +32,9 @@ EXPORTED = [
     "fa8_static_scratch_bytes",
     "fa8_lse_merge",
     "fa8_quantize_e4m3",
+    "fa8_bwd_params_init",
+    "fa8_bwd_workspace_size",
+    "fa8_bwd",
     "fa8_status_string",
     "fa8_last_error_message",
     "fa8_launch_count",
@@ -67,6 +70,19 @@ class Fa8FwdParams(C.Structure):
     ]
 
 
+class Fa8BwdParams(C.Structure):
+    """Mirror of ``struct fa8_bwd_params``."""
+    _fields_ = [
+        ("batch", C.c_int64), ("heads", C.c_int64), ("heads_kv", C.c_int64),
+        ("seqlen_q", C.c_int64), ("seqlen_kv", C.c_int64), ("head_dim", C.c_int64),
+        ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("o", C.c_void_p),
+        ("d_o", C.c_void_p), ("lse", C.c_void_p),
+        ("dq", C.c_void_p), ("dk", C.c_void_p), ("dv", C.c_void_p),
+        ("causal", C.c_int32), ("softmax_scale", C.c_float), ("v_layout", C.c_int32),
+        ("status", C.c_void_p), ("timeout_cycles", C.c_longlong),
+    ]
+
+
 _lib = None
 
 
@@ -93,6 +109,12 @@ def lib(path: Path | None = None) -> C.CDLL:
         L.fa8_quantize_e4m3.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int64, C.c_int64,
                                         C.c_int64, C.c_float, C.c_int, C.c_void_p]
         L.fa8_quantize_e4m3.restype = C.c_int
+        L.fa8_bwd_params_init.argtypes = [C.POINTER(Fa8BwdParams)] + [C.c_int64] * 6
+        L.fa8_bwd_params_init.restype = None
+        L.fa8_bwd_workspace_size.argtypes = [C.POINTER(Fa8BwdParams)]
+        L.fa8_bwd_workspace_size.restype = C.c_int64
+        L.fa8_bwd.argtypes = [C.POINTER(Fa8BwdParams), C.c_void_p, C.c_int64, C.c_void_p]
+        L.fa8_bwd.restype = C.c_int
         L.fa8_status_string.argtypes = [C.c_int]
         L.fa8_status_string.restype = C.c_char_p
         L.fa8_last_error_message.argtypes = []
@@ -145,3 +167,18 @@ def quantize_e4m3(x_ptr, in_dtype, y_ptr, batch, rows, cols, scale, transpose,
                   stream: int = 0) -> int:
     return lib().fa8_quantize_e4m3(x_ptr, in_dtype, y_ptr, batch, rows, cols, scale,
                                    int(transpose), C.c_void_p(stream))
+
+
+def bwd_params(batch, heads, heads_kv, seqlen_q, seqlen_kv, head_dim) -> Fa8BwdParams:
+    p = Fa8BwdParams()
+    lib().fa8_bwd_params_init(C.byref(p), batch, heads, heads_kv, seqlen_q, seqlen_kv, head_dim)
+    return p
+
+
+def bwd_workspace_size(p: Fa8BwdParams) -> int:
+    """Device workspace bytes fa8_bwd needs for these parameters (-1: invalid)."""
+    return int(lib().fa8_bwd_workspace_size(C.byref(p)))
+
+
+def bwd(p: Fa8BwdParams, workspace: int, workspace_bytes: int, stream: int = 0) -> int:
+    return lib().fa8_bwd(C.byref(p), C.c_void_p(workspace), workspace_bytes, C.c_void_p(stream))

@@ -96,3 +96,28 @@ def test_aux_entry_points_validate(abi):
     assert abi.lse_merge([0x1000], 1, [0x2000], 10, 128, 0x1008, 128, None) == abi.FA8_ERR_ALIGNMENT
     assert abi.quantize_e4m3(None, 0, 0x1000, 1, 1, 16, 1.0, 0) == abi.FA8_ERR_INVALID_ARG
     assert abi.lib().fa8_status_string(3) == b"alignment / stride requirement violated"
+
+
+def test_bwd_params_struct_layout_matches_c(abi, tmp_path):
+    src = tmp_path / "layout_bwd.c"
+    fields = [f[0] for f in abi.Fa8BwdParams._fields_]
+    body = "\n".join(f'  printf("{f} %zu\\n", offsetof(fa8_bwd_params, {f}));' for f in fields)
+    src.write_text(f'#include <stdio.h>\n#include <stddef.h>\n#include "fa8.h"\nint main(void){{\n'
+                   f'  printf("size %zu\\n", sizeof(fa8_bwd_params));\n{body}\n  return 0;\n}}\n')
+    exe = tmp_path / "layout_bwd"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    lines = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True,
+                                                    text=True).stdout.splitlines())
+    assert int(lines["size"]) == C.sizeof(abi.Fa8BwdParams)
+    for f in fields:
+        assert int(lines[f]) == getattr(abi.Fa8BwdParams, f).offset, f
+
+
+def test_bwd_params_and_workspace_size(abi):
+    p = abi.bwd_params(2, 8, 4, 100, 300, 128)
+    assert p.causal == 1 and p.v_layout == abi.FA8_V_BHDS and p.softmax_scale == 0.0
+    # fp16 copies of Q (2*8*128*128), K and V (2*4*384*128 each), Delta (2*8*128 floats)
+    assert abi.bwd_workspace_size(p) == 2 * 8 * 128 * 128 * 2 + 2 * (2 * 4 * 384 * 128 * 2) + 2 * 8 * 128 * 4
+    p.head_dim = 96
+    assert abi.bwd_workspace_size(p) == -1
+    assert abi.bwd(p, 0, 0) == abi.FA8_ERR_UNSUPPORTED

@@ -158,3 +158,32 @@ def test_split_kv_needs_a_workspace(abi, cuda):
     p.kv_splits = 0
     assert abi.fwd(p) == abi.FA8_OK  # automatic: falls back to no split
     torch.cuda.synchronize()
+
+
+def test_cabi_backward_matches_torch_entry(abi, cuda):
+    """fa8_bwd called through ctypes with a caller-owned workspace gives the
+    same gradients as the torch entry point (same kernels), bit for bit."""
+    import torch
+    import ada_cute_fp8_flash_attention_b200 as fa8
+    B, H, Hkv, S, D = 1, 4, 2, 256, 128
+    q, k, v = U.inputs(B, H, Hkv, S, S, D, "normal", seed=21)
+    qd, kd, vd = U.to_dev(q, cuda), U.to_dev(k, cuda), U.to_dev(v, cuda)
+    o, lse = fa8.flash_attn_fp8_forward_ex(qd, kd, vd, causal=True, return_lse=True)
+    g = torch.Generator(device=cuda).manual_seed(3)
+    d_o = torch.randn((B, H, S, D), device=cuda, generator=g).to(torch.float16)
+    want = fa8.flash_attn_fp8_backward(qd, kd, vd, o, d_o, lse, causal=True)
+    p = abi.bwd_params(B, H, Hkv, S, S, D)
+    grads = [torch.empty((B, H, S, D), dtype=torch.float32, device=cuda),
+             torch.empty((B, Hkv, S, D), dtype=torch.float32, device=cuda),
+             torch.empty((B, Hkv, S, D), dtype=torch.float32, device=cuda)]
+    p.q, p.k, p.v, p.o, p.d_o = qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(), d_o.data_ptr()
+    p.lse = lse.data_ptr()
+    p.dq, p.dk, p.dv = (t.data_ptr() for t in grads)
+    nbytes = abi.bwd_workspace_size(p)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
+    abi.check(abi.bwd(p, ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    for got, exp in zip(grads, want):
+        assert torch.equal(got, exp)
+    # a workspace one byte short is refused
+    assert abi.bwd(p, ws.data_ptr(), nbytes - 1, 0) == abi.FA8_ERR_INVALID_ARG
