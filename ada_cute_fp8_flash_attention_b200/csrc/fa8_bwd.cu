@@ -635,8 +635,8 @@ int check(const fa8_bwd_params* p) {
     return fa8_note_error(FA8_ERR_INVALID_ARG, "fa8_bwd: bad sizes (heads % heads_kv != 0?)");
   if (p->v_layout != FA8_V_BHDS && p->v_layout != FA8_V_BHSD)
     return fa8_note_error(FA8_ERR_INVALID_ARG, "fa8_bwd: bad v_layout");
-  if (p->batch > 65535 || p->heads > 65535)
-    return fa8_note_error(FA8_ERR_UNSUPPORTED, "fa8_bwd: batch / heads above the grid limit");
+  if (p->batch > 65535 || p->heads > 65535 || p->batch * p->heads > 65535)
+    return fa8_note_error(FA8_ERR_UNSUPPORTED, "fa8_bwd: batch x heads above the grid limit");
   return FA8_OK;
 }
 
@@ -743,6 +743,19 @@ int fa8_bwd(const fa8_bwd_params* p, void* workspace, int64_t workspace_bytes, v
   int rc = check(p);
   if (rc != FA8_OK) return rc;
   if (p->batch == 0 || (p->seqlen_q == 0 && p->seqlen_kv == 0)) return FA8_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p->seqlen_q == 0 || p->seqlen_kv == 0) {
+    // No query sees a key: every gradient is zero (no workspace needed).
+    const size_t q_bytes = (size_t)(p->batch * p->heads * p->seqlen_q * p->head_dim) * 4;
+    const size_t kv_bytes = (size_t)(p->batch * p->heads_kv * p->seqlen_kv * p->head_dim) * 4;
+    if ((q_bytes && !p->dq) || (kv_bytes && (!p->dk || !p->dv)))
+      return fa8_note_error(FA8_ERR_INVALID_ARG, "fa8_bwd: null gradient pointer");
+    cudaError_t e = cudaSuccess;
+    if (q_bytes) e = cudaMemsetAsync(p->dq, 0, q_bytes, st);
+    if (e == cudaSuccess && kv_bytes) e = cudaMemsetAsync(p->dk, 0, kv_bytes, st);
+    if (e == cudaSuccess && kv_bytes) e = cudaMemsetAsync(p->dv, 0, kv_bytes, st);
+    return e == cudaSuccess ? FA8_OK : fa8_note_cuda_error(e, "fa8_bwd (empty sequence)");
+  }
   if (!p->q || !p->k || !p->v || !p->o || !p->d_o || !p->lse || !p->dq || !p->dk || !p->dv)
     return fa8_note_error(FA8_ERR_INVALID_ARG, "fa8_bwd: null tensor pointer");
   if (!workspace || workspace_bytes < ws_layout(p).total ||
@@ -754,7 +767,6 @@ int fa8_bwd(const fa8_bwd_params* p, void* workspace, int64_t workspace_bytes, v
   for (const void* q : ptrs16)
     if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0)
       return fa8_note_error(FA8_ERR_ALIGNMENT, "fa8_bwd: d_o, dq, dk, dv must be 16-byte aligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   return p->head_dim == 64 ? launch<64>(p, workspace, st) : launch<128>(p, workspace, st);
 }
 

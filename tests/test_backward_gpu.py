@@ -74,3 +74,19 @@ def test_backward_deterministic():
     b = _run(1, 2, 2, 256, 256, 128, True, seed=3)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("Sq,Skv", [(0, 128), (128, 0)])
+def test_backward_empty_sequences_give_zero_gradients(Sq, Skv):
+    import ada_cute_fp8_flash_attention_b200 as fa8
+    dev = torch.device("cuda:0")
+    q = torch.zeros((1, 2, Sq, 64), device=dev).to(torch.float8_e4m3fn)
+    k = torch.zeros((1, 2, Skv, 64), device=dev).to(torch.float8_e4m3fn)
+    v = torch.zeros((1, 2, 64, Skv), device=dev).to(torch.float8_e4m3fn)
+    o = torch.zeros((1, 2, Sq, 64), device=dev, dtype=torch.float16)
+    lse = torch.full((1, 2, Sq), float("-inf"), device=dev)
+    dq, dk, dv = fa8.flash_attn_fp8_backward(q, k, v, o, o.clone(), lse, causal=False)
+    torch.cuda.synchronize()
+    assert dq.shape == (1, 2, Sq, 64) and dk.shape == (1, 2, Skv, 64)
+    for t in (dq, dk, dv):
+        assert t.numel() == 0 or bool((t == 0).all())
