@@ -272,7 +272,10 @@ __global__ void __launch_bounds__(kThreadsTile, 1)
   const uint32_t sb = ptx::smem_u32(smem);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   // Fixed tile: blockIdx.x = tile, y = head (K/V head for dK/dV), z = batch.
-  const int fx = blockIdx.x, hy = blockIdx.y, b = blockIdx.z;
+  // Causal dQ: query tile i streams i + 1 key tiles, so the grid runs the
+  // last (heaviest) tiles first; dK/dV's heaviest tiles are already the first.
+  const int fx = (kDq && p.causal) ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+  const int hy = blockIdx.y, b = blockIdx.z;
   int n_iter, i_lo = 0;
   if constexpr (kDq) {
     const int nkv = (p.skv + kTile - 1) / kTile;
