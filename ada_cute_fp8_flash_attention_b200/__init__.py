@@ -60,7 +60,7 @@ def flash_attn_fp8_forward(q, k, v):
 def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout="bhds",
                               return_lse=False, out_dtype="fp16", q_offset=0, kv_offset=0,
                               split_keys=-1, out=None, lse=None, descale_q=1.0, descale_k=1.0,
-                              descale_v=1.0):
+                              descale_v=1.0, sm_budget=0):
     """FP8 attention forward with options.
 
     Returns ``out`` or ``(out, lse)`` when ``return_lse`` is set. ``lse`` is the
@@ -71,7 +71,9 @@ def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout
     lo) e4m3 P; -1 = default (1024), 0 = never. ``descale_q/k/v``: dequantisation
     factors of scaled e4m3 inputs (real value = code x factor), each a float
     (per tensor) or a device tensor that broadcasts to (B, H) for Q and to
-    (B, H_kv) for K and V (per batch and head).
+    (B, H_kv) for K and V (per batch and head). ``sm_budget`` > 0 runs the kernel
+    on at most that many SMs (a multiple of 8) of a green-context partition,
+    leaving the rest to concurrent work such as NCCL transfers; 0 = whole GPU.
     """
     import torch
 
@@ -80,7 +82,7 @@ def flash_attn_fp8_forward_ex(q, k, v, causal=True, softmax_scale=None, v_layout
     (sq, tq), (sk, tk), (sv, tv) = split(descale_q), split(descale_k), split(descale_v)
     res = _C.flash_attn_fp8_forward_ex(q, k, v, causal, softmax_scale, v_layout, return_lse,
                                        out_dtype, q_offset, kv_offset, split_keys, out, lse,
-                                       sq, sk, sv, tq, tk, tv)
+                                       sq, sk, sv, tq, tk, tv, int(sm_budget))
     return (res[0], res[1]) if return_lse else res[0]
 
 

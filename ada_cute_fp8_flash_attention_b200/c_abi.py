@@ -55,7 +55,7 @@ class Fa8FwdParams(C.Structure):
         ("softmax_scale", C.c_float), ("causal", C.c_int32), ("v_layout", C.c_int32),
         ("out_dtype", C.c_int32),
         ("q_offset", C.c_int64), ("kv_offset", C.c_int64),
-        ("split_keys", C.c_int32), ("reserved2", C.c_int32),
+        ("split_keys", C.c_int32), ("sm_budget", C.c_int32),
         ("descale_q", C.c_float), ("descale_k", C.c_float), ("descale_v", C.c_float),
         ("reserved0", C.c_int32),
         ("cu_seqlens_q", C.c_void_p), ("cu_seqlens_kv", C.c_void_p),

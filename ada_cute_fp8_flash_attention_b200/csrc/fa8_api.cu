@@ -21,7 +21,9 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "../../include/fa8.h"
 #include "fa8_fwd_kernel.cuh"
@@ -87,6 +89,66 @@ int setup_kernel_attr(int dev) {
                                      fa8::TileCfg<D>::kSmemAlloc);
   });
   if (errs[dev] != cudaSuccess) return set_cuda_error(errs[dev], "cudaFuncSetAttribute");
+  return FA8_OK;
+}
+
+// SM budget: a stream of a green context that owns `want` SMs (a multiple of
+// 8, the partition granularity on sm_90+), created once per (device, count)
+// and kept for the life of the process. *out = nullptr when the budget covers
+// the whole GPU (launch on the caller's stream).
+template <typename F>
+F driver_fn(const char* name) {
+  void* ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion(name, &ptr, 12080, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<F>(ptr);
+}
+
+int budget_stream(int dev, int n_sms, cudaStream_t* out) {
+  *out = nullptr;
+  int total = 0;
+  cudaError_t ce = cudaDeviceGetAttribute(&total, cudaDevAttrMultiProcessorCount, dev);
+  if (ce != cudaSuccess) return set_cuda_error(ce, "cudaDeviceGetAttribute (SM count)");
+  const int want = (n_sms + 7) / 8 * 8;
+  if (want >= total) return FA8_OK;
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, cudaStream_t> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, want});
+  if (it != cache.end()) {
+    *out = it->second;
+    return FA8_OK;
+  }
+  auto get_dev = driver_fn<decltype(&cuDeviceGet)>("cuDeviceGet");
+  auto get_res = driver_fn<decltype(&cuDeviceGetDevResource)>("cuDeviceGetDevResource");
+  auto split = driver_fn<decltype(&cuDevSmResourceSplitByCount)>("cuDevSmResourceSplitByCount");
+  auto gen = driver_fn<decltype(&cuDevResourceGenerateDesc)>("cuDevResourceGenerateDesc");
+  auto mk_ctx = driver_fn<decltype(&cuGreenCtxCreate)>("cuGreenCtxCreate");
+  auto mk_stream = driver_fn<decltype(&cuGreenCtxStreamCreate)>("cuGreenCtxStreamCreate");
+  if (!get_dev || !get_res || !split || !gen || !mk_ctx || !mk_stream)
+    return set_msg(FA8_ERR_DRIVER, "sm_budget: green-context driver entry points not found");
+  CUdevice cu_dev;
+  CUdevResource all, grp, rem;
+  CUdevResourceDesc desc;
+  CUgreenCtx gctx;
+  CUstream cs;
+  unsigned int n_groups = 1;
+  CUresult r = get_dev(&cu_dev, dev);
+  if (r == CUDA_SUCCESS) r = get_res(cu_dev, &all, CU_DEV_RESOURCE_TYPE_SM);
+  if (r == CUDA_SUCCESS) r = split(&grp, &n_groups, &all, &rem, 0, (unsigned)want);
+  if (r == CUDA_SUCCESS && n_groups < 1) r = CUDA_ERROR_INVALID_VALUE;
+  if (r == CUDA_SUCCESS) r = gen(&desc, &grp, 1);
+  if (r == CUDA_SUCCESS) r = mk_ctx(&gctx, desc, cu_dev, CU_GREEN_CTX_DEFAULT_STREAM);
+  if (r == CUDA_SUCCESS) r = mk_stream(&cs, gctx, CU_STREAM_NON_BLOCKING, 0);
+  if (r != CUDA_SUCCESS) {
+    snprintf(g_last_msg, sizeof(g_last_msg), "sm_budget: green context of %d SMs failed (CUresult %d)",
+             want, (int)r);
+    return FA8_ERR_DRIVER;
+  }
+  cache[{dev, want}] = reinterpret_cast<cudaStream_t>(cs);
+  *out = reinterpret_cast<cudaStream_t>(cs);
   return FA8_OK;
 }
 
@@ -366,7 +428,29 @@ int fa8_fwd(const fa8_fwd_params* p, void* stream) {
       sp = SplitPlan();  // automatic: run without splitting
     }
   }
-  return p->head_dim == 128 ? launch<128>(p, s, dev, sp) : launch<64>(p, s, dev, sp);
+  if (p->sm_budget < 0) return set_msg(FA8_ERR_INVALID_ARG, "sm_budget must be >= 0");
+  cudaStream_t ls = nullptr;
+  if (p->sm_budget > 0) {
+    const int rc = budget_stream(dev, p->sm_budget, &ls);
+    if (rc != FA8_OK) return rc;
+  }
+  if (!ls) return p->head_dim == 128 ? launch<128>(p, s, dev, sp) : launch<64>(p, s, dev, sp);
+  // Budgeted launch: ordered after the caller's stream and before its next work.
+  cudaEvent_t e_in = nullptr, e_out = nullptr;
+  e = cudaEventCreateWithFlags(&e_in, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&e_out, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventRecord(e_in, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(ls, e_in, 0);
+  int rc = FA8_ERR_CUDA;
+  if (e == cudaSuccess) {
+    rc = p->head_dim == 128 ? launch<128>(p, ls, dev, sp) : launch<64>(p, ls, dev, sp);
+    e = cudaEventRecord(e_out, ls);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, e_out, 0);
+  }
+  if (e_in) cudaEventDestroy(e_in);
+  if (e_out) cudaEventDestroy(e_out);
+  if (e != cudaSuccess) return set_cuda_error(e, "sm_budget stream ordering");
+  return rc;
 }
 
 int64_t fa8_fwd_workspace_size(const fa8_fwd_params* p) {

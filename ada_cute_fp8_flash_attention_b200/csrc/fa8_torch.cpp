@@ -56,7 +56,8 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
                                         double descale_v = 1.0,
                                         c10::optional<torch::Tensor> descale_q_bh = c10::nullopt,
                                         c10::optional<torch::Tensor> descale_k_bh = c10::nullopt,
-                                        c10::optional<torch::Tensor> descale_v_bh = c10::nullopt) {
+                                        c10::optional<torch::Tensor> descale_v_bh = c10::nullopt,
+                                        int64_t sm_budget = 0) {
   check_fp8_input(q, "q");
   check_fp8_input(k, "k");
   check_fp8_input(v, "v");
@@ -177,6 +178,8 @@ std::vector<torch::Tensor> forward_impl(torch::Tensor q, torch::Tensor k, torch:
   p.descale_q_stride_h = 1;
   p.descale_kv_stride_b = Hkv;
   p.descale_kv_stride_h = 1;
+  TORCH_CHECK(sm_budget >= 0, "sm_budget must be >= 0");
+  p.sm_budget = (int32_t)sm_budget;
   // Split-KV for calls too small to fill the GPU: a workspace from the caching
   // allocator whose leading counters start at zero.
   torch::Tensor ws;
@@ -209,14 +212,15 @@ std::vector<torch::Tensor> flash_attn_fp8_forward_ex(
     std::string out_dtype, int64_t q_offset, int64_t kv_offset, int64_t split_keys,
     c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> lse, double descale_q,
     double descale_k, double descale_v, c10::optional<torch::Tensor> descale_q_bh,
-    c10::optional<torch::Tensor> descale_k_bh, c10::optional<torch::Tensor> descale_v_bh) {
+    c10::optional<torch::Tensor> descale_k_bh, c10::optional<torch::Tensor> descale_v_bh,
+    int64_t sm_budget) {
   TORCH_CHECK(q.dim() == 4, "q must be (B, H, S, D)");
   const double scale = softmax_scale.has_value()
                            ? *softmax_scale
                            : 1.0 / std::sqrt(static_cast<double>(q.size(3)));
   return forward_impl(q, k, v, causal, scale, v_layout, return_lse, out_dtype, q_offset,
                       kv_offset, split_keys, out, lse, descale_q, descale_k, descale_v,
-                      descale_q_bh, descale_k_bh, descale_v_bh);
+                      descale_q_bh, descale_k_bh, descale_v_bh, sm_budget);
 }
 
 // Variable-length (packed) batches: q (total_q, H, D), k (total_kv, H_kv, D),
@@ -440,7 +444,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("split_keys") = -1, py::arg("out") = py::none(), py::arg("lse") = py::none(),
         py::arg("descale_q") = 1.0, py::arg("descale_k") = 1.0, py::arg("descale_v") = 1.0,
         py::arg("descale_q_bh") = py::none(), py::arg("descale_k_bh") = py::none(),
-        py::arg("descale_v_bh") = py::none(),
+        py::arg("descale_v_bh") = py::none(), py::arg("sm_budget") = 0,
         "FP8 attention forward with options; returns [out] or [out, lse]");
   m.def("flash_attn_fp8_varlen_forward", &flash_attn_fp8_varlen_forward, py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("cu_seqlens_q"), py::arg("cu_seqlens_kv"),

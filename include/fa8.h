@@ -100,8 +100,12 @@ typedef struct fa8_fwd_params {
    * whose first row sees fewer than this many keys; -1 selects the default
    * (1024), 0 disables the split. */
   int32_t split_keys;
-  /* Reserved (set to 0). */
-  int32_t reserved2;
+  /* SM budget: > 0 runs the kernel on at most this many SMs (rounded up to a
+   * multiple of 8) through a green-context stream that the library creates
+   * once per device and count, ordered after `stream` and before its later
+   * work; it leaves the other SMs to concurrent kernels (e.g. the NCCL
+   * transfers of a context-parallel exchange). 0 = the whole GPU. */
+  int32_t sm_budget;
 
   /* Per-tensor dequantisation factors of e4m3 Q, K, V (real value = code x
    * factor); 1.0 = unscaled inputs. The kernel folds descale_q * descale_k

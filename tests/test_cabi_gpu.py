@@ -187,3 +187,35 @@ def test_cabi_backward_matches_torch_entry(abi, cuda):
         assert torch.equal(got, exp)
     # a workspace one byte short is refused
     assert abi.bwd(p, ws.data_ptr(), nbytes - 1, 0) == abi.FA8_ERR_INVALID_ARG
+
+
+def test_cabi_sm_budget_same_output_on_fewer_sms(abi, cuda):
+    """sm_budget runs the forward on a green-context partition of the GPU:
+    bit-identical output, ordered on the caller's stream, and slower when it
+    gets fewer than half of the SMs."""
+    import torch
+    B, H, S, D = 1, 32, 4096, 128
+    q, k, v = U.inputs(B, H, H, S, S, D, "normal", seed=5)
+    qd, kd, vd = U.to_dev(q, cuda), U.to_dev(k, cuda), U.to_dev(v, cuda)
+    outs, times = [], []
+    for budget in (0, 32, 0, 32):
+        out = torch.zeros((B, H, S, D), dtype=torch.float16, device=cuda)
+        p = abi.params(B, H, H, S, S, D)
+        p.q, p.k, p.v, p.o = qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr()
+        p.sm_budget = budget
+        stream = torch.cuda.current_stream()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        abi.check(abi.fwd(p, stream.cuda_stream))
+        b.record(stream)
+        out.add_(0)  # later work on the caller's stream sees the finished output
+        torch.cuda.synchronize()
+        outs.append(out)
+        times.append(a.elapsed_time(b))
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    assert times[3] > 1.6 * times[2], times
+    p = abi.params(B, H, H, S, S, D)
+    p.q, p.k, p.v, p.o = qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), outs[0].data_ptr()
+    p.sm_budget = -1
+    assert abi.fwd(p, 0) == abi.FA8_ERR_INVALID_ARG

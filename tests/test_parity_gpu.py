@@ -348,3 +348,16 @@ def test_causal_with_unequal_lengths(fa8, cuda, Sq, Skv, D):
     fin = np.isfinite(l_ref)
     assert np.array_equal(np.isfinite(l), fin)
     assert np.abs(l[fin] - l_ref[fin]).max() < 1e-3
+
+
+def test_sm_budget_through_torch_is_bit_identical(cuda):
+    import torch
+    import ada_cute_fp8_flash_attention_b200 as fa8
+    q, k, v = U.inputs(2, 4, 4, 512, 512, 128, "normal", seed=9)
+    qd, kd, vd = U.to_dev(q, cuda), U.to_dev(k, cuda), U.to_dev(v, cuda)
+    a = fa8.flash_attn_fp8_forward_ex(qd, kd, vd, causal=True)
+    b = fa8.flash_attn_fp8_forward_ex(qd, kd, vd, causal=True, sm_budget=16)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    with pytest.raises(RuntimeError):
+        fa8.flash_attn_fp8_forward_ex(qd, kd, vd, causal=True, sm_budget=-1)
