@@ -131,14 +131,14 @@ ComputeFn = Callable[..., Tuple[object, object]]  # (q, k, v_bhds, q_off, kv_off
 MergeFn = Callable[[Sequence[object], Sequence[object]], Tuple[object, object]]
 
 
-def _default_compute(softmax_scale: Optional[float]):
+def _default_compute(softmax_scale: Optional[float], sm_budget: int = 0):
     from . import flash_attn_fp8_forward_ex
 
     def compute(q, k, v_bhds, q_off, kv_off):
         # fp32 partial output: rounded only once, by the merge
         return flash_attn_fp8_forward_ex(q, k, v_bhds, causal=True, softmax_scale=softmax_scale,
                                          v_layout="bhds", return_lse=True, out_dtype="fp32",
-                                         q_offset=q_off, kv_offset=kv_off)
+                                         q_offset=q_off, kv_offset=kv_off, sm_budget=sm_budget)
     return compute
 
 
@@ -151,7 +151,8 @@ def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
                    softmax_scale: Optional[float] = None,
                    compute: Optional[ComputeFn] = None, merge: Optional[MergeFn] = None,
                    schedule: str = "allgather",
-                   deadline_s: Optional[float] = DEFAULT_DEADLINE_S):
+                   deadline_s: Optional[float] = DEFAULT_DEADLINE_S,
+                   sm_budget: int = 0):
     """Causal attention of this rank's zig-zag Q chunks against the whole sequence.
 
     q_loc, k_loc: (B, H, 2*chunk, D) e4m3 — this rank's chunks (split_local, dim 2);
@@ -166,7 +167,8 @@ def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
     collective bandwidth, so "allgather" is the faster schedule there.
 
     deadline_s bounds every wait on the exchange (CPTimeoutError after it);
-    None waits without a bound.
+    None waits without a bound. sm_budget > 0 runs the attention kernels on
+    that many SMs, leaving the rest to NCCL's transfer kernels.
     """
     import torch
     import torch.distributed as dist
@@ -175,7 +177,7 @@ def ring_attention(q_loc, k_loc, v_loc_bhds, zz: ZigZag, rank: int, group=None,
         raise ValueError(f"context parallel supports at most {MAX_MERGE_PARTS // 2} ranks "
                          f"(rank 0 merges 2 x world partial outputs, the merge takes "
                          f"{MAX_MERGE_PARTS}); got world = {zz.world}")
-    compute = compute or _default_compute(softmax_scale)
+    compute = compute or _default_compute(softmax_scale, sm_budget)
     merge = merge or _default_merge
     if schedule == "allgather":
         return _allgather_attention(q_loc, k_loc, v_loc_bhds, zz, rank, group, compute, merge,
